@@ -1,0 +1,396 @@
+"""Benchmark of flicker's DiT attention hot path on B200: qk_prep -> attend.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config 1024|512|2048] [--shard batch|heads]
+
+One step = one pass of the hot path over one attention call's inputs: the
+fused QKV [B, S, 3*24*128] bf16 -> qk_prep (QK-RMSNorm + RoPE + q gain, head
+transpose) -> attend (bounded flash attention) -> o [B, 24, S, 128] bf16.
+The default workload is the 1024x1024 image call (S = 4608 = 512 text + 4096
+image tokens, 24 heads, head_dim 128, batch 1), seeded synthetic inputs with
+the reference configs' distributions.
+
+Metric: attend TFLOP/s (4*B*H*S^2*D algorithmic FLOPs per step) over the whole
+step, with qk_prep's HBM GB/s and each kernel's roofline fraction reported
+beside it. Rank 0 prints one JSON line.
+
+Multi-GPU (torchrun, one process per GPU, NCCL):
+  --shard batch  (default) each rank runs its own batch element (config 2:
+                 batch 8 over 8 GPUs, seed = rank); no data-path collective;
+                 weak scaling.
+  --shard heads  one batch-1 call split by heads (24/N per rank), followed by
+                 an NCCL all-gather of the attention output; strong scaling.
+
+--impl reference times the reference's plain-XLA path restated on the host
+cores (jax is not installable, see oracle/cpu_baseline.py) on the same config.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "attend TFLOP/s + qk_prep HBM GB/s @1024² (S=4608,H=24,D=128) vs roofline"
+NUM_HEADS = 24
+HEAD_DIM = 128
+NUM_TXT = 512
+GRIDS = {"512": (32, 32), "1024": (64, 64), "2048": (128, 128)}
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(GRIDS), default="1024")
+    ap.add_argument("--shard", choices=["batch", "heads"], default="batch")
+    ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end leg (default K/10)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-heads", type=int, default=4, help="heads in the CPU-baseline sample")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {k: float(p[k]) for k in FALLBACK_PEAKS}, "measured"
+    except (OSError, KeyError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def qk_prep_bytes(b, s, h, d=HEAD_DIM):
+    """Algorithmic HBM bytes of one qk_prep call: read qkv + write q,k,v + fp32 tables + 2 scale vectors."""
+    return 2 * (b * s * 3 * h * d * 2) + 2 * s * d * 4 + 2 * d * 2
+
+
+def attend_flops(b, s, h, d=HEAD_DIM):
+    return 4.0 * b * h * s * s * d
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clock/throttle samples of one GPU while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        time.sleep(0.25)
+        self.summary = {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        if self.proc is None:
+            return False
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = []
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[4:]))
+            except ValueError:
+                continue
+        if not rows:
+            self.summary["reasons"] = ["no samples"]
+            return False
+        loaded = [r for r in rows if r[2] > 250.0] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in loaded for i, flag in enumerate(r[3][1:5]) if flag.lower() == "active"})
+        self.summary = {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                        "reasons": reasons, "samples": len(loaded)}
+        return False
+
+
+# ------------------------------------------------------------------ inputs
+def make_inputs(torch, config, batch, heads, seed, device):
+    """Seeded synthetic inputs: qkv ~ N(0,1) bf16, scales ~ U(0.5,1.5) bf16, joint RoPE lane tables."""
+    from flicker_b200 import kernels, rope
+
+    gh, gw = GRIDS[config]
+    s = NUM_TXT + gh * gw
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    qkv = torch.randn((batch, s, 3 * heads * HEAD_DIM), generator=g, device=device,
+                      dtype=torch.float32).to(torch.bfloat16)
+    gs = torch.Generator(device=device)
+    gs.manual_seed(seed + 1)
+    q_scale = (torch.rand(HEAD_DIM, generator=gs, device=device) + 0.5).to(torch.bfloat16)
+    k_scale = (torch.rand(HEAD_DIM, generator=gs, device=device) + 0.5).to(torch.bfloat16)
+    pe = rope.joint_pe(NUM_TXT, gh, gw, device=device)
+    freqs = kernels.lane_pair(pe, 1.0 / math.sqrt(HEAD_DIM))
+    return qkv, q_scale, k_scale, freqs
+
+
+# ------------------------------------------------------------------ reference arm / CPU leg
+def cpu_sample(config, n_heads, reps=1):
+    """Time the CPU restatement of the reference's XLA path on `n_heads` heads of `config`."""
+    import torch
+
+    from oracle import cpu_baseline, restatement as R
+
+    gh, gw = GRIDS[config]
+    s = NUM_TXT + gh * gw
+    qkv = torch.from_numpy(R.make_qkv(1, s, NUM_HEADS, HEAD_DIM, 0).view("int16")).view(torch.bfloat16)
+    qs, ks = R.make_scales()
+    q_scale = torch.from_numpy(qs.view("int16")).view(torch.bfloat16)
+    k_scale = torch.from_numpy(ks.view("int16")).view(torch.bfloat16)
+    pe = torch.from_numpy(R.joint_pe(gh, gw))
+    times, flops, threads = [], 0.0, 1
+    for r in range(reps):
+        h0 = (r * n_heads) % NUM_HEADS
+        heads = range(h0, min(NUM_HEADS, h0 + n_heads))
+        dt, fl, threads = cpu_baseline.time_heads(qkv, q_scale, k_scale, pe, NUM_HEADS, heads)
+        times.append(dt)
+        flops = fl
+    return times, flops, threads, s
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    n_heads = 1
+    steps, warmup = max(1, args.steps), max(0, args.warmup)
+    # Bound the arm to a few minutes: one head per step, at most 40 timed steps.
+    steps_run = min(steps, 40)
+    warm_run = min(warmup, 3)
+    cpu_sample(args.config, n_heads, reps=warm_run) if warm_run else None
+    times, flops, threads, s = cpu_sample(args.config, n_heads, reps=steps_run)
+    total = sum(times)
+    value = flops * len(times) / total / 1e12
+    sample = (f"{steps_run} steps x 1 head of {NUM_HEADS} (batch 1, S={s}); plain-XLA path "
+              f"(heads, rms_norm, apply_rope, sdpa) restated in torch fp32 on host cores")
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": steps_run,
+        "warmup": warm_run, "ms_per_step": 1e3 * total / len(times), "higher_is_better": True,
+        "scaling": "weak" if args.shard == "batch" else "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": f"flicker {args.config}^2 attention call: qk_prep + attend", "batch": 1,
+                   "seq_len": s, "heads": NUM_HEADS, "head_dim": HEAD_DIM},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ our arm
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import flicker_b200 as fb
+    from flicker_b200 import sharding
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    group = dist.group.WORLD if world > 1 else None
+
+    heads_total = NUM_HEADS
+    if args.shard == "heads" and world > 1:
+        h0, h1 = sharding.head_range(heads_total, world, rank)
+    else:
+        h0, h1 = 0, heads_total
+    heads_local = h1 - h0
+    seed = rank if (args.shard == "batch" and world > 1) else 0
+
+    sets = []
+    for i in range(2):  # two input sets, alternated, so no step finds its qkv in L2
+        qkv, qs, ks, freqs = make_inputs(torch, args.config, 1, heads_total, seed + 100 * i, dev)
+        if heads_local != heads_total:
+            qkv = sharding.slice_qkv_heads(qkv, heads_total, h0, h1)
+        sets.append((qkv.contiguous(), qs, ks, freqs))
+    s = sets[0][0].shape[1]
+    flops_local = attend_flops(1, s, heads_local)
+    bytes_local = qk_prep_bytes(1, s, heads_local)
+
+    gathered = None
+    if args.shard == "heads" and world > 1:
+        gathered = torch.empty((world, 1, heads_local, s, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+
+    def step(i, rec=None):
+        qkv, qs, ks, freqs = sets[i % 2]
+        if rec is not None:
+            rec[0].record()
+        q, k, v = fb.qk_prep(qkv, qs, ks, freqs, heads_local)
+        if rec is not None:
+            rec[1].record()
+        o = fb.attend(q, k, v)
+        if rec is not None:
+            rec[2].record()
+        if gathered is not None:
+            sharding.gather_heads(o, gathered, group)
+        return o
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize()
+    if fb.device_status() != 0:
+        raise RuntimeError("device status reports a timed-out wait during warm-up")
+
+    K = args.steps
+    recs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for i in range(K):
+            step(i, recs[i])
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    elapsed_ms = start.elapsed_time(end)
+    qk_ms = statistics.mean(r[0].elapsed_time(r[1]) for r in recs)
+    at_ms = statistics.mean(r[1].elapsed_time(r[2]) for r in recs)
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    status = fb.device_status()
+
+    # ---- end-to-end leg: host buffers through the public API, copies inside the timed region
+    e2e_steps = args.e2e_steps or max(3, K // 10)
+    qkv0, qs0, ks0, freqs0 = sets[0]
+    h_qkv = qkv0.cpu().pin_memory()
+    h_tab = [t.cpu().pin_memory() for t in (freqs0.cos, freqs0.sin)]
+    h_sc = [t.cpu().pin_memory() for t in (qs0, ks0)]
+    h_out = torch.empty((1, heads_total if gathered is not None else heads_local, s, HEAD_DIM),
+                        dtype=torch.bfloat16).pin_memory()
+    d_qkv = torch.empty_like(qkv0)
+    d_tab = [torch.empty_like(freqs0.cos), torch.empty_like(freqs0.sin)]
+    d_sc = [torch.empty_like(qs0), torch.empty_like(ks0)]
+
+    def e2e_step():
+        d_qkv.copy_(h_qkv, non_blocking=True)
+        for d, h in zip(d_tab + d_sc, h_tab + h_sc):
+            d.copy_(h, non_blocking=True)
+        q, k, v = fb.qk_prep(d_qkv, d_sc[0], d_sc[1], fb.Freqs(d_tab[0], d_tab[1], freqs0.q_gain), heads_local)
+        o = fb.attend(q, k, v)
+        if gathered is not None:
+            sharding.gather_heads(o, gathered, group)
+            h_out.copy_(gathered.view(h_out.shape), non_blocking=True)
+        else:
+            h_out.copy_(o, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d = h_qkv.numel() * 2 + sum(t.numel() * t.element_size() for t in h_tab + h_sc)
+    d2h = h_out.numel() * 2
+
+    pk, pk_kind = peaks()
+    total_flops = flops_local * world if (args.shard == "batch" or world == 1) else attend_flops(1, s, heads_total)
+    value = total_flops * K / (elapsed_ms * 1e-3) / 1e12
+    e2e_value = total_flops * e2e_steps / (e2e_ms * 1e-3) / 1e12
+    at_tflops = flops_local / (at_ms * 1e-3) / 1e12
+    qk_gbs = bytes_local / (qk_ms * 1e-3) / 1e9
+
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": K,
+            "warmup": max(3, args.warmup), "ms_per_step": elapsed_ms / K, "higher_is_better": True,
+            "scaling": "weak" if (args.shard == "batch" or world == 1) else "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {
+                "workload": f"flicker {args.config}^2 attention call: qk_prep + attend",
+                "batch": world if (args.shard == "batch" and world > 1) else 1,
+                "seq_len": s, "heads": heads_total, "head_dim": HEAD_DIM,
+                "parallelism": (f"batch{world}" if args.shard == "batch" else f"heads{world}+allgather")
+                if world > 1 else "single",
+                "l2": "2 alternating input sets; per-step footprint (qkv + q,k,v + o) > 126 MB L2",
+            },
+            "kernels": {
+                "qk_prep": {"us": qk_ms * 1e3, "GB/s": qk_gbs, "bytes": bytes_local,
+                            "frac_hbm": qk_gbs / pk["hbm_gbs"]},
+                "attend": {"us": at_ms * 1e3, "TFLOP/s": at_tflops, "flops": flops_local,
+                           "frac_bf16": at_tflops / pk["bf16_tflops"],
+                           "frac_bf16_spec_2250": at_tflops / 2250.0},
+            },
+            "roofline": {"bound": "tensor", "achieved": at_tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": at_tflops / pk["bf16_tflops"], "traffic": None,
+                         "peak_source": f"{pk_kind} bf16 burst (cuBLAS)", "kernel": "attend"},
+            "roofline_qk_prep": {"bound": "hbm", "achieved": qk_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                 "frac": qk_gbs / pk["hbm_gbs"], "traffic": None,
+                                 "peak_source": f"{pk_kind} HBM copy"},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "steps": e2e_steps, "ms_per_step": e2e_ms / e2e_steps},
+            "gpu_launches": 2 * K,
+            "clocks": clocks.summary,
+            "device_status": status,
+        }
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            times, fl, threads, _ = cpu_sample(args.config, args.cpu_heads, reps=1)
+            line["cpu_baseline"] = {
+                "value": fl / times[0] / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                "sample": f"{args.cpu_heads} of {NUM_HEADS} heads, batch 1, S={s}: plain-XLA path restated in "
+                          f"torch fp32 (heads, rms_norm, apply_rope, sdpa)"}
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,339 @@
+// Bounded (max-free) flash attention for sm_100a: TMA -> shared memory -> tcgen05.mma -> TMEM.
+//
+// Restates flicker kernels.attend (src/flicker/kernels.py:105-145):
+//   s = q k^T (fp32, q already carries 1/sqrt(D)),  p = bf16(exp(s)),
+//   l += sum fp32(p),  acc += p v (fp32),  o = bf16(acc / l) once at the end.
+// There is no running max and hence no rescaling of acc: the accumulator stays in
+// tensor memory for the whole KV loop and is read exactly once, in the epilogue.
+//
+// One CTA owns two 128-row query tiles of one (batch, head) and walks all KV blocks
+// of 128 rows. Warp roles (320 threads, 1 CTA per SM):
+//   warp 0      TMA producer: Q tiles once, then K_j, V_j into a 4-slot ring of 32 KB slots
+//   warp 1      TMEM allocator + single-thread UMMA issuer
+//   warps 2-5   "softmax" for query tile 0, warps 6-9 for query tile 1: one thread per
+//               query row (TMEM lane), exp + bf16 round + row sum, P written back to TMEM,
+//               then the epilogue O / l -> bf16 -> global.
+// TMEM (512 columns x 128 lanes, fp32): S_t at columns [128t, 128t+128) for t = 0, 1, with
+// P_t (bf16, two per column) written over the first 64 of them; O_t at [256+128t, ...).
+// Per KV block the issuer runs, in order:
+//   PV_0(j) [needs P_0(j)], S_0(j+1), PV_1(j) [needs P_1(j)], S_1(j+1)
+// so one tile's exp overlaps the other tile's two GEMMs. UMMAs from one thread execute
+// in issue order, which is what makes writing S_t(j+1) over P_t(j) safe.
+// Shared-memory operands use the 128-byte swizzle written by TMA: Q and K are K-major
+// (head dim contiguous), V is the MN-major B operand of P.V (head dim contiguous).
+// No TMA multicast is used anywhere.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "flicker_b200.h"
+#include "ptx.cuh"
+
+namespace flk {
+
+namespace {
+
+constexpr int kTile = 128;                 // query rows per tile, KV rows per block
+constexpr int kDim = 128;                  // head dim
+constexpr int kSlots = 4;                  // K/V ring slots
+constexpr int kTileBytes = kTile * kDim * 2;  // 32 KB: one bf16 128 x 128 tile
+constexpr int kHalfBytes = kTileBytes / 2;    // one 64-column TMA box (128 B rows)
+constexpr int kThreads = 320;
+constexpr uint32_t kTmemCols = 512;
+constexpr float kLog2e = 1.4426950408889634f;
+
+constexpr uint32_t kIdescQK = umma_idesc_bf16_f32(128, 128, false);
+constexpr uint32_t kIdescPV = umma_idesc_bf16_f32(128, 128, true);
+
+struct alignas(1024) Smem {
+  uint8_t q[2][kTileBytes];
+  uint8_t kv[kSlots][kTileBytes];
+  uint64_t q_full;
+  uint64_t kv_full[kSlots];
+  uint64_t kv_empty[kSlots];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_full[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+struct Params {
+  int S;         // sequence length (multiple of 128)
+  int n_tiles;   // S / 128
+  uint16_t* o;   // [B*H*S, 128] bf16
+  int* status;   // device status word
+};
+
+__device__ __forceinline__ Smem* smem_ptr(uint8_t* raw) {
+  const uintptr_t a = (reinterpret_cast<uintptr_t>(raw) + 1023) & ~static_cast<uintptr_t>(1023);
+  return reinterpret_cast<Smem*>(a);
+}
+
+// K-major operand (rows of 128 bf16 split in two 64-column swizzled boxes): K-chunk kc of 16.
+__device__ __forceinline__ uint64_t desc_kmajor(const uint8_t* tile, int kc) {
+  return umma_desc_sw128(smem_u32(tile) + (kc >> 2) * kHalfBytes + (kc & 3) * 32, 16, 1024);
+}
+// MN-major B operand (V): K-chunk kc = KV rows [16kc, 16kc+16); N = head dim over both boxes.
+__device__ __forceinline__ uint64_t desc_mnmajor(const uint8_t* tile, int kc) {
+  return umma_desc_sw128(smem_u32(tile) + kc * 2048, kHalfBytes, 1024);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attend_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_v, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& sm = *smem_ptr(smem_raw);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int bh = blockIdx.y;
+  const int t0 = blockIdx.x * 2;
+  const int nt = min(2, p.n_tiles - t0);
+  const int n_kv = p.n_tiles;
+  const int row_base = bh * p.S;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&sm.kv_full[s], 1);
+      mbar_init(&sm.kv_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&sm.s_full[t], 1);
+      mbar_init(&sm.p_full[t], 128);
+      mbar_init(&sm.o_full[t], 1);
+    }
+    mbar_init(&sm.drain, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  volatile int* abort = &sm.abort;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ TMA producer
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      mbar_arrive_expect_tx(&sm.q_full, nt * kTileBytes);
+      for (int t = 0; t < nt; ++t) {
+        const int row = row_base + (t0 + t) * kTile;
+        tma_load_2d(sm.q[t], &tm_q, 0, row, &sm.q_full);
+        tma_load_2d(sm.q[t] + kHalfBytes, &tm_q, 64, row, &sm.q_full);
+      }
+      int issued[kSlots] = {0, 0, 0, 0};
+      for (int n = 0; n < 2 * n_kv; ++n) {
+        const int slot = n % kSlots;
+        const int use = n / kSlots;
+        if (use > 0 && !mbar_wait(&sm.kv_empty[slot], (use - 1) & 1, abort, p.status)) break;
+        mbar_arrive_expect_tx(&sm.kv_full[slot], kTileBytes);
+        const void* map = (n & 1) ? static_cast<const void*>(&tm_v) : static_cast<const void*>(&tm_k);
+        const int row = row_base + (n >> 1) * kTile;
+        tma_load_2d(sm.kv[slot], map, 0, row, &sm.kv_full[slot]);
+        tma_load_2d(sm.kv[slot] + kHalfBytes, map, 64, row, &sm.kv_full[slot]);
+        issued[slot] = use + 1;
+      }
+      // Never leave with a copy in flight: wait (bounded) for the last fill of every slot.
+      mbar_wait(&sm.q_full, 0, abort, p.status);
+      for (int s = 0; s < kSlots; ++s)
+        if (issued[s] > 0) mbar_wait(&sm.kv_full[s], (issued[s] - 1) & 1, abort, p.status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ UMMA issuer
+      bool ok = mbar_wait(&sm.q_full, 0, abort, p.status);
+      tc_fence_after();
+      auto kv_ready = [&](int n) {
+        return mbar_wait(&sm.kv_full[n % kSlots], (n / kSlots) & 1, abort, p.status);
+      };
+      // S_t(0) = Q_t K_0^T
+      if (ok) ok = kv_ready(0);
+      if (ok) {
+        tc_fence_after();
+        const uint8_t* kt = sm.kv[0];
+        for (int t = 0; t < nt; ++t) {
+#pragma unroll
+          for (int kc = 0; kc < 8; ++kc)
+            umma_ss(tmem + t * 128, desc_kmajor(sm.q[t], kc), desc_kmajor(kt, kc), kIdescQK, kc > 0);
+          tc_commit(&sm.s_full[t]);
+        }
+        tc_commit(&sm.kv_empty[0]);
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int nv = 2 * j + 1, nk = 2 * j + 2;
+        const bool last = (j == n_kv - 1);
+        ok = kv_ready(nv);
+        if (!ok) break;
+        tc_fence_after();
+        const uint8_t* vt = sm.kv[nv % kSlots];
+        const uint8_t* kt = sm.kv[nk % kSlots];
+        for (int t = 0; t < nt; ++t) {
+          ok = mbar_wait(&sm.p_full[t], j & 1, abort, p.status);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int kc = 0; kc < 8; ++kc)
+            umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kc * 8, desc_mnmajor(vt, kc), kIdescPV,
+                    (j > 0 || kc > 0) ? 1u : 0u);
+          if (last) {
+            tc_commit(&sm.o_full[t]);
+          } else {
+            if (t == 0) {
+              ok = kv_ready(nk);
+              if (!ok) break;
+              tc_fence_after();
+            }
+#pragma unroll
+            for (int kc = 0; kc < 8; ++kc)
+              umma_ss(tmem + t * 128, desc_kmajor(sm.q[t], kc), desc_kmajor(kt, kc), kIdescQK, kc > 0);
+            tc_commit(&sm.s_full[t]);
+          }
+        }
+        if (!ok) break;
+        tc_commit(&sm.kv_empty[nv % kSlots]);
+        if (!last) tc_commit(&sm.kv_empty[nk % kSlots]);
+      }
+      // Drain: every UMMA issued above has completed before TMEM is released.
+      tc_commit(&sm.drain);
+      mbar_wait(&sm.drain, 0, abort, p.status);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int t = (warp - 2) >> 2;
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;
+    if (t < nt) {
+      const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+      const uint32_t s_addr = tmem + lane_off + t * 128;
+      float l = 0.f;
+      bool ok = true;
+      for (int j = 0; j < n_kv; ++j) {
+        // Warp-uniform outcome: the tcgen05.ld/st below are .sync.aligned.
+        ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_full[t], j & 1, abort, p.status));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(s_addr + c * 32, r);
+          tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float e0 = ex2_approx(__uint_as_float(r[2 * i]) * kLog2e);
+            const float e1 = ex2_approx(__uint_as_float(r[2 * i + 1]) * kLog2e);
+            pk[i] = pack_bf16x2(e0, e1);
+            l += __uint_as_float(pk[i] << 16) + __uint_as_float(pk[i] & 0xFFFF0000u);
+          }
+          tmem_st_32x32b_x16(s_addr + c * 16, pk);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&sm.p_full[t]);
+      }
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.o_full[t], 0, abort, p.status));
+      if (ok) {
+        tc_fence_after();
+        const uint32_t o_addr = tmem + lane_off + 256 + t * 128;
+        uint16_t* orow = p.o + (static_cast<size_t>(row_base) + (t0 + t) * kTile + row) * kDim;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(o_addr + c * 32, r);
+          tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pk[i] = pack_bf16x2(__fdiv_rn(__uint_as_float(r[2 * i]), l),
+                                __fdiv_rn(__uint_as_float(r[2 * i + 1]), l));
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- host side
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// [rows, 128] bf16 row-major viewed through 64-column x 128-row boxes with the 128-byte swizzle.
+static bool make_tile_map(CUtensorMap* map, const void* base, long long rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kDim), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kDim) * 2};
+  const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kTile)};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static size_t attend_smem_bytes() { return sizeof(Smem) + 1024; }
+
+int launch_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, uint16_t* o,
+                  int* status, cudaStream_t stream) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return FLK_ERR_CUDA;
+  static bool configured[64] = {};
+  if (dev < 0 || dev >= 64) return FLK_ERR_UNSUPPORTED;
+  if (!configured[dev]) {
+    if (cudaFuncSetAttribute(attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(attend_smem_bytes())) != cudaSuccess)
+      return FLK_ERR_CUDA;
+    configured[dev] = true;
+  }
+  const long long rows = static_cast<long long>(B) * H * S;
+  CUtensorMap mq, mk, mv;
+  if (!make_tile_map(&mq, q, rows) || !make_tile_map(&mk, k, rows) || !make_tile_map(&mv, v, rows))
+    return FLK_ERR_CUDA;
+  Params p;
+  p.S = S;
+  p.n_tiles = S / kTile;
+  p.o = o;
+  p.status = status;
+  const dim3 grid((p.n_tiles + 1) / 2, B * H);
+  attend_kernel<<<grid, kThreads, attend_smem_bytes(), stream>>>(mq, mk, mv, p);
+  return cudaGetLastError() == cudaSuccess ? FLK_OK : FLK_ERR_CUDA;
+}
+
+}  // namespace flk

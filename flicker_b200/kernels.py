@@ -1,0 +1,177 @@
+"""flicker's hot-path kernel API (``flicker.kernels``) on B200.
+
+Same names, argument meanings and error behaviour as the reference module
+``src/flicker/kernels.py``; arrays are CUDA ``torch.Tensor`` s instead of jax
+arrays, and the work runs in the sm_100a kernels of ``libflicker_b200.so``
+(through its C ABI) on the tensor's device and current torch stream.
+
+* ``qk_prep`` -- kernels.py:57-91 (fused head split + QK-RMSNorm + RoPE + q gain)
+* ``attend``  -- kernels.py:105-145 (bounded, max-free flash attention)
+* ``Freqs``, ``EPS``, ``ROW_TILES``, ``row_tile``, ``lane_pair``, ``SCORE_TILES``,
+  ``EXP_LIMIT``, ``logit_bound`` -- kernels.py:12-31,94-101
+
+There is no CPU or eager fallback: if the library is missing the call raises.
+"""
+from __future__ import annotations
+
+import math
+from typing import NamedTuple
+
+import numpy as np
+import torch
+
+from . import _lib
+
+Array = torch.Tensor
+
+
+class Freqs(NamedTuple):
+    """kernels.py:12-16: RoPE lane tables ``cos``/``sin`` [L, 128] fp32 and the q gain."""
+
+    cos: Array
+    sin: Array
+    q_gain: float = 1.0
+
+
+EPS = 1e-6
+ROW_TILES = (2304, 1536, 1152, 512, 256, 128, 64)
+SCORE_TILES = (2304, 1536, 1152, 512, 256, 128)
+EXP_LIMIT = 80.0
+HEAD_DIM = 128
+
+
+def row_tile(length: int) -> int | None:
+    """kernels.py:23-24: first row tile that divides ``length``, or None."""
+    return next((size for size in ROW_TILES if length % size == 0), None)
+
+
+def lane_pair(freqs: Array, q_gain: float = 1.0) -> Freqs:
+    """kernels.py:28-31: RoPE table [1, 1, L, 64, 2, 2] -> lane tables [L, 128].
+
+    cos lanes repeat cos(theta) twice; sin lanes interleave (-sin, +sin), so the
+    rotation is ``cos * x + sin * pair_swap(x)``.
+    """
+    cos, sin = freqs[..., 0, 0][0, 0], freqs[..., 1, 0][0, 0]
+    lanes = torch.stack([-sin, sin], dim=-1).reshape(*sin.shape[:-1], 2 * sin.shape[-1])
+    return Freqs(torch.repeat_interleave(cos, 2, dim=-1).contiguous(), lanes.contiguous(), q_gain)
+
+
+def logit_bound(q_scale, k_scale):
+    """kernels.py:99-101: sqrt(D) * max|q_scale| * max|k_scale| along the last axis."""
+    if isinstance(q_scale, torch.Tensor):
+        width = q_scale.shape[-1]
+        return math.sqrt(width) * q_scale.float().abs().amax(-1) * k_scale.float().abs().amax(-1)
+    q_scale, k_scale = np.asarray(q_scale, np.float32), np.asarray(k_scale, np.float32)
+    width = q_scale.shape[-1]
+    return np.float32(math.sqrt(width)) * np.max(np.abs(q_scale), -1) * np.max(np.abs(k_scale), -1)
+
+
+def _stream(t: Array) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _require_cuda_bf16(name: str, t: Array) -> None:
+    if not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (this package has no CPU path)")
+    if t.dtype != torch.bfloat16:
+        raise ValueError(f"{name} must be bfloat16, got {t.dtype}")
+
+
+def qk_prep(
+    qkv: Array,
+    q_scale: Array,
+    k_scale: Array,
+    freqs: Freqs,
+    num_heads: int,
+    *,
+    rows: int | None = None,
+    interpret: bool = False,
+) -> tuple[Array, Array, Array]:
+    """Fused head transpose + QK-RMSNorm + RoPE (+ q gain) in one HBM pass.
+
+    ``qkv`` [B, L, 3*H*D] bf16 (columns ordered (3, H, D)) -> q, k, v [B, H, L, D] bf16.
+    ``q = bf16(q_gain * rope(fp32(bf16(rmsnorm(x)) * q_scale)))``, k likewise without the
+    gain, v copied (kernels.py:35-53). ``rows`` is the reference's row-tile hint: it is
+    validated exactly as kernels.py:71-73 does (``ValueError`` when no tile divides L);
+    the CUDA kernel does not need a row tile. ``interpret`` (Pallas interpret mode in the
+    reference) is not available.
+    """
+    if interpret:
+        raise NotImplementedError("interpret=True: this build runs only the sm_100a kernels")
+    _require_cuda_bf16("qkv", qkv)
+    if qkv.dim() != 3:
+        raise ValueError(f"qkv must be [B, L, 3*H*D], got shape {tuple(qkv.shape)}")
+    batch, length, width = qkv.shape
+    if num_heads <= 0 or width % (3 * num_heads):
+        raise ValueError(f"width {width} is not 3 * num_heads * head_dim for num_heads={num_heads}")
+    head_dim = width // (3 * num_heads)
+    tile_rows = rows or row_tile(length)
+    if tile_rows is None or length % tile_rows:
+        raise ValueError(f"qk_prep needs a row tile dividing L={length} (rows={tile_rows})")
+    if head_dim != HEAD_DIM:
+        raise ValueError(f"head_dim must be {HEAD_DIM}, got {head_dim}")
+    cos, sin, q_gain = freqs
+    for name, t in (("freqs.cos", cos), ("freqs.sin", sin)):
+        if not isinstance(t, torch.Tensor) or t.device != qkv.device or t.dtype != torch.float32:
+            raise ValueError(f"{name} must be a float32 tensor on {qkv.device}")
+        if tuple(t.shape) != (length, head_dim):
+            raise ValueError(f"{name} must be [L, {head_dim}] = [{length}, {head_dim}], got {tuple(t.shape)}")
+    scales = []
+    for name, t in (("q_scale", q_scale), ("k_scale", k_scale)):
+        _require_cuda_bf16(name, t)
+        if t.numel() != head_dim or t.device != qkv.device:
+            raise ValueError(f"{name} must hold {head_dim} values on {qkv.device}")
+        scales.append(t.reshape(head_dim).contiguous())
+    qkv = qkv.contiguous()
+    cos, sin = cos.contiguous(), sin.contiguous()
+    out = [torch.empty((batch, num_heads, length, head_dim), dtype=qkv.dtype, device=qkv.device)
+           for _ in range(3)]
+    with torch.cuda.device(qkv.device):
+        code = _lib.lib().flk_qk_prep(
+            qkv.data_ptr(), scales[0].data_ptr(), scales[1].data_ptr(), cos.data_ptr(), sin.data_ptr(),
+            float(q_gain), batch, length, num_heads, head_dim,
+            out[0].data_ptr(), out[1].data_ptr(), out[2].data_ptr(), _stream(qkv))
+    _lib.check("flk_qk_prep", code)
+    return out[0], out[1], out[2]
+
+
+def attend(q: Array, k: Array, v: Array, *, block: int | None = None, interpret: bool = False) -> Array:
+    """Bounded flash attention without a running max; q already carries 1/sqrt(D).
+
+    q, k, v [B, H, S, D] bf16 -> o [B, H, S, D] bf16 with
+    ``o = bf16((sum_j bf16(exp(q k_j^T)) v_j) / sum_j fp32(bf16(exp(q k_j^T))))``
+    (kernels.py:113-130). ``block`` is the reference's score-tile hint; it must divide S
+    and be a multiple of 128 (the kernel's own KV block). S must be a multiple of 128:
+    the reference raises from ``next()`` there, this raises ``ValueError``.
+    """
+    if interpret:
+        raise NotImplementedError("interpret=True: this build runs only the sm_100a kernels")
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _require_cuda_bf16(name, t)
+        if t.dim() != 4 or tuple(t.shape) != tuple(q.shape) or t.device != q.device:
+            raise ValueError(f"q, k, v must share one [B, H, S, D] shape and device; {name} is "
+                             f"{tuple(t.shape)}")
+    batch, heads, length, dim = q.shape
+    if dim != HEAD_DIM:
+        raise ValueError(f"head_dim must be {HEAD_DIM}, got {dim}")
+    if length % 128:
+        raise ValueError(f"attend needs S to be a multiple of 128, got {length}")
+    if block is not None and (block <= 0 or block % 128 or length % block):
+        raise ValueError(f"block={block} must be a multiple of 128 dividing S={length}")
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    o = torch.empty_like(q)
+    lib = _lib.lib()
+    with torch.cuda.device(q.device):
+        ws_bytes = lib.flk_attend_workspace_size(batch, heads, length, dim)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
+        code = lib.flk_attend(q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, length, dim,
+                              o.data_ptr(), ws.data_ptr() if ws is not None else None, ws_bytes,
+                              _stream(q))
+    _lib.check("flk_attend", code)
+    return o
+
+
+def device_status(device: torch.device | int | None = None) -> int:
+    """Synchronise ``device`` and return (and clear) the kernels' device status word (0 = ok)."""
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        return _lib.lib().flk_device_status()

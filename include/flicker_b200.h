@@ -1,0 +1,94 @@
+/*
+ * flicker_b200 -- C ABI of the B200 (sm_100a) kernels for flicker's DiT attention hot path.
+ *
+ * Plain pointers and sizes only. Every tensor argument is a DEVICE pointer
+ * into memory of the current CUDA device; bf16 tensors are passed as their
+ * 16-bit patterns (uint16_t). `stream` is a cudaStream_t (NULL = legacy
+ * default stream). Entry points enqueue work and return immediately; they
+ * never synchronise, never allocate device memory, never abort or trap.
+ *
+ * Return codes: 0 on success, a negative FLK_ERR_* code otherwise
+ * (flk_error_string() names it). A kernel that detects a problem while it
+ * runs (a bounded wait that ran out) records it in a device-side status word
+ * that flk_device_status() reads back.
+ *
+ * Layouts (row-major, contiguous):
+ *   qkv      [B, L, 3*H*D]  columns ordered (3, H, D): q heads, then k heads, then v heads
+ *   q, k, v  [B, H, L, D]   head-major
+ *   o        [B, H, S, D]
+ *   cos, sin [L, D] fp32    lane tables: cos[l, 2j] = cos[l, 2j+1] = cos(theta_lj),
+ *                           sin[l, 2j] = -sin(theta_lj), sin[l, 2j+1] = +sin(theta_lj)
+ * D must be 128.
+ */
+#ifndef FLICKER_B200_H
+#define FLICKER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FLK_OK 0
+#define FLK_ERR_INVALID_ARGUMENT (-1)  /* bad shape, null pointer or misaligned pointer */
+#define FLK_ERR_UNSUPPORTED (-2)       /* shape this build does not support (e.g. D != 128) */
+#define FLK_ERR_CUDA (-3)              /* a CUDA runtime/driver call failed (e.g. launch) */
+#define FLK_ERR_WORKSPACE (-4)         /* workspace missing or smaller than required */
+#define FLK_ERR_DEVICE_TIMEOUT (-5)    /* device status: a bounded in-kernel wait ran out */
+#define FLK_ERR_NO_DEVICE (-6)         /* current device is not sm_100 */
+
+/*
+ * Fused head split + QK-RMSNorm + RoPE (+ q gain) for one attention call.
+ * Replaces flicker kernels.qk_prep (src/flicker/kernels.py:57-91, body :35-53):
+ *   q[b,h,l,:] = bf16(q_gain * rope(fp32(bf16(rmsnorm(x_q)) * q_scale)))
+ *   k[b,h,l,:] = bf16(rope(fp32(bf16(rmsnorm(x_k)) * k_scale)))
+ *   v[b,h,l,:] = x_v
+ * rmsnorm(x) = x * rsqrt(mean(x^2) + 1e-6) in fp32; the bf16 multiply by the
+ * scale rounds to bf16; rope(w)[i] = cos[l,i]*w[i] + sin[l,i]*w[i^1].
+ * q_scale, k_scale: [D] bf16. Pointers 16-byte aligned.
+ */
+int flk_qk_prep(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t* k_scale,
+                const float* cos, const float* sin, float q_gain,
+                int B, int L, int H, int D,
+                uint16_t* q, uint16_t* k, uint16_t* v, void* stream);
+
+/*
+ * Bounded (max-free) non-causal attention, q pre-scaled by 1/sqrt(D).
+ * Replaces flicker kernels.attend (src/flicker/kernels.py:105-145):
+ *   p = bf16(exp(q k^T)),  l = sum_j fp32(p_j),  o = bf16((sum_j p_j v_j) / l)
+ * S must be a multiple of 128. `workspace`/`ws_bytes` is scratch the caller
+ * owns; flk_attend_workspace_size() says how much a call needs (0 when the
+ * call runs unsplit, in which case workspace may be NULL).
+ */
+int flk_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+               int B, int H, int S, int D, uint16_t* o,
+               void* workspace, size_t ws_bytes, void* stream);
+
+/* Bytes of workspace flk_attend needs for this shape on the current device. */
+size_t flk_attend_workspace_size(int B, int H, int S, int D);
+
+/*
+ * Load-time guard of the max-free softmax. Replaces kernels.logit_bound
+ * (src/flicker/kernels.py:99-101) and the refusal in loader.check_logit_bound
+ * (src/flicker/loader.py:115-128): returns sqrt(D) * max|q_scale| * max|k_scale|
+ * for fp32 host arrays of length D in *bound, and FLK_OK when it is below
+ * EXP_LIMIT = 80, FLK_ERR_INVALID_ARGUMENT otherwise. Host-only, no GPU work.
+ */
+int flk_logit_bound(const float* q_scale, const float* k_scale, int D, float* bound);
+
+/* Reads (and clears) the device-side status word of the current device: 0 or FLK_ERR_DEVICE_TIMEOUT.
+ * Synchronises the device. */
+int flk_device_status(void);
+
+/* Human-readable name of a FLK_* return code. */
+const char* flk_error_string(int code);
+
+/* ABI version of this library (major * 100 + minor). */
+int flk_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLICKER_B200_H */

@@ -1,0 +1,128 @@
+"""attend on the B200 against the oracle and the reference-code golden vectors (through the C ABI)."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN_CASES, bit_equal_fraction, load_golden, to_device, to_host
+from oracle import restatement as R
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+import flicker_b200 as fb  # noqa: E402
+
+
+def run_attend(q, k, v):
+    o = fb.attend(to_device(q), to_device(k), to_device(v))
+    torch.cuda.synchronize()
+    return to_host(o)
+
+
+def random_qkv(b, h, s, seed, scale=1.0):
+    """q with 1/sqrt(D) folded in and k, v ~ N(0, 1) (the post-qk_prep statistics)."""
+    rng = np.random.default_rng(seed)
+    q = R.bf16(rng.standard_normal((b, h, s, 128), dtype=np.float32) * np.float32(scale / math.sqrt(128)))
+    k = R.bf16(rng.standard_normal((b, h, s, 128), dtype=np.float32))
+    v = R.bf16(rng.standard_normal((b, h, s, 128), dtype=np.float32))
+    return q, k, v
+
+
+@pytest.mark.parametrize("name", GOLDEN_CASES)
+def test_golden(name):
+    g = load_golden(name)
+    o = run_attend(g["q"], g["k"], g["v"])
+    assert R.within_tolerance(o, g["o"].astype(np.float32))
+    assert bit_equal_fraction(o, g["o"]) > 0.95
+    assert R.within_tolerance(o, g["o_xla"].astype(np.float32))
+    assert R.within_tolerance(o, R.attention_fp32(g["q"], g["k"], g["v"]))
+
+
+@pytest.mark.parametrize("b,h,s", [(1, 1, 128), (1, 2, 256), (1, 1, 384), (2, 3, 640), (1, 4, 1152)])
+def test_small_shapes_all_rows(b, h, s):
+    q, k, v = random_qkv(b, h, s, seed=s + h)
+    o = run_attend(q, k, v)
+    want = R.attend_kernel(q, k, v, block=128)
+    assert bit_equal_fraction(o, want) > 0.95
+    assert R.within_tolerance(o, R.attention_fp32(q, k, v))
+
+
+@pytest.mark.parametrize("config,rows_per_head", [("512", None), ("1024", 96), ("2048", 32)])
+def test_config_pipeline(config, rows_per_head):
+    """qk_prep -> attend on a named config vs the reference's plain-XLA path and the kernel path."""
+    qkv, qs, ks, pe, freqs = R.make_config(config)
+    f = fb.Freqs(to_device(freqs.cos), to_device(freqs.sin), freqs.q_gain)
+    qd, kd, vd = fb.qk_prep(to_device(qkv), to_device(qs), to_device(ks), f, R.NUM_HEADS)
+    o = to_host(fb.attend(qd, kd, vd))
+    q, k, v = to_host(qd), to_host(kd), to_host(vd)
+    length = q.shape[2]
+    rng = np.random.default_rng(0)
+    heads = range(R.NUM_HEADS) if rows_per_head is None or config != "2048" else (0, 11, 23)
+    for h in heads:
+        rows = np.arange(length) if rows_per_head is None else np.sort(
+            rng.choice(length, rows_per_head, replace=False))
+        got = o[:, h:h + 1, rows]
+        want32 = R.attention_fp32(q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1], rows)
+        assert R.within_tolerance(got, want32), (h, R.compare(got, want32))
+        kern = R.attend_kernel(q[:, h:h + 1], k[:, h:h + 1], v[:, h:h + 1], block=128, rows=rows)
+        assert bit_equal_fraction(got, kern) > 0.95
+    if config != "2048":
+        # Whole-call check against the reference's XLA path on the same inputs (sampled rows).
+        xq, xk, xv = R.qkv_prep_xla(qkv, qs, ks, pe, R.NUM_HEADS)
+        rows = np.sort(rng.choice(length, 64, replace=False))
+        want = R.sdpa(xq, xk, xv, rows=rows)
+        assert R.within_tolerance(o[:, :, rows], want.astype(np.float32))
+    assert fb.device_status() == 0
+
+
+def test_scaling_v_by_two_is_exact():
+    """Linearity in v with a power-of-two factor: o(2v) == 2 o(v) bit for bit."""
+    q, k, v = random_qkv(1, 2, 512, seed=5)
+    o1 = run_attend(q, k, v)
+    o2 = run_attend(q, k, R.bf16(v.astype(np.float32) * 2))
+    np.testing.assert_array_equal(o2.astype(np.float32), o1.astype(np.float32) * 2)
+
+
+def test_constant_v_rows_reproduce_v():
+    """A convex combination of identical rows is that row (up to fp32 sum order of l vs acc)."""
+    q, k, _ = random_qkv(1, 2, 1024, seed=6)
+    rng = np.random.default_rng(1)
+    row = R.bf16(rng.standard_normal(128).astype(np.float32))
+    v = np.broadcast_to(row, (1, 2, 1024, 128)).copy()
+    o = run_attend(q, k, v)
+    assert R.within_tolerance(o, v.astype(np.float32))
+    assert bit_equal_fraction(o, v) > 0.98
+
+
+def test_large_logits_within_bound():
+    """Logits up to ~60 (inside EXP_LIMIT = 80): exp stays finite and results stay correct."""
+    q, k, v = random_qkv(1, 1, 512, seed=8, scale=5.0)
+    o = run_attend(q, k, v)
+    assert np.isfinite(o.astype(np.float32)).all()
+    assert R.within_tolerance(o, R.attention_fp32(q, k, v))
+
+
+def test_deterministic():
+    q, k, v = random_qkv(1, 3, 1024, seed=9)
+    a = run_attend(q, k, v)
+    b = run_attend(q, k, v)
+    assert bit_equal_fraction(a, b) == 1.0
+
+
+def test_api_errors_on_device():
+    q = torch.zeros(1, 2, 100, 128, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError, match="multiple of 128"):
+        fb.attend(q, q, q)
+    q = torch.zeros(1, 2, 256, 64, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError, match="head_dim"):
+        fb.attend(q, q, q)
+    q = torch.zeros(1, 2, 256, 128, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ValueError, match="block"):
+        fb.attend(q, q, q, block=192)
+    with pytest.raises(ValueError, match="shape"):
+        fb.attend(q, q[:, :1], q)
+    o = fb.attend(q, q, q, block=256)
+    assert o.shape == q.shape
+    assert fb.device_status() == 0

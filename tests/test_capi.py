@@ -1,0 +1,101 @@
+"""The C-ABI library: it loads, exports every symbol include/*.h declares, and its host-side
+checks answer without touching a GPU (no compute is launched in these tests)."""
+from __future__ import annotations
+
+import ctypes
+import glob
+import os
+import re
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+from flicker_b200 import _lib
+
+
+def declared_functions() -> set[str]:
+    names = set()
+    for header in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        text = open(header).read()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names |= set(re.findall(r"\b(flk_\w+)\s*\(", text))
+    return names
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert {"flk_qk_prep", "flk_attend", "flk_attend_workspace_size", "flk_logit_bound",
+            "flk_device_status", "flk_error_string", "flk_abi_version"} <= names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.lib()
+    missing = [n for n in sorted(declared_functions()) if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(_lib.SIGNATURES) == declared_functions()
+
+
+def test_library_has_sm100a_code():
+    """The shared object carries an sm_100a fatbin (read through the toolkit's own listing tool)."""
+    import shutil
+    import subprocess
+
+    tool = shutil.which("cuobjdump") or "/usr/local/cuda/bin/cuobjdump"
+    if not os.path.exists(tool):
+        pytest.skip("cuobjdump not available")
+    res = subprocess.run([tool, "--list-elf", _lib.LIB_PATH], capture_output=True, text=True)
+    assert "sm_100a" in res.stdout
+
+
+def test_error_strings_and_version():
+    lib = _lib.lib()
+    assert lib.flk_abi_version() >= 100
+    for code in (0, -1, -2, -3, -4, -5, -6):
+        assert lib.flk_error_string(code)
+    assert b"unknown" in lib.flk_error_string(-99)
+
+
+def test_logit_bound_host_entry_point():
+    lib = _lib.lib()
+    fp = ctypes.POINTER(ctypes.c_float)
+    q = np.full(128, 1.5, np.float32)
+    k = np.full(128, 1.5, np.float32)
+    out = ctypes.c_float()
+    code = lib.flk_logit_bound(q.ctypes.data_as(fp), k.ctypes.data_as(fp), 128, ctypes.byref(out))
+    assert code == 0 and abs(out.value - np.sqrt(128) * 2.25) < 1e-4
+    k[3] = -3.0  # |scale| counts
+    code = lib.flk_logit_bound(q.ctypes.data_as(fp), k.ctypes.data_as(fp), 128, ctypes.byref(out))
+    assert code == 0 and abs(out.value - np.sqrt(128) * 4.5) < 1e-4
+    q[:] = 5.0
+    code = lib.flk_logit_bound(q.ctypes.data_as(fp), k.ctypes.data_as(fp), 128, ctypes.byref(out))
+    assert code == _lib.FLK_ERR_INVALID_ARGUMENT and out.value >= 80.0
+    assert lib.flk_logit_bound(None, k.ctypes.data_as(fp), 128, ctypes.byref(out)) == _lib.FLK_ERR_INVALID_ARGUMENT
+
+
+def test_shape_checks_run_before_any_device_work():
+    """Invalid shapes are refused on the host with an error code (never a launch)."""
+    lib = _lib.lib()
+    fake = ctypes.c_void_p(0x10000)  # aligned, never dereferenced: the shape check fails first
+    # head_dim != 128
+    assert lib.flk_qk_prep(fake, fake, fake, fake, fake, 1.0, 1, 64, 2, 64, fake, fake, fake, None) \
+        == _lib.FLK_ERR_UNSUPPORTED
+    assert lib.flk_attend(fake, fake, fake, 1, 2, 128, 64, fake, None, 0, None) == _lib.FLK_ERR_UNSUPPORTED
+    # S not a multiple of 128
+    assert lib.flk_attend(fake, fake, fake, 1, 2, 100, 128, fake, None, 0, None) \
+        == _lib.FLK_ERR_INVALID_ARGUMENT
+    # negative sizes / bad head count
+    assert lib.flk_qk_prep(fake, fake, fake, fake, fake, 1.0, -1, 64, 2, 128, fake, fake, fake, None) \
+        == _lib.FLK_ERR_INVALID_ARGUMENT
+    assert lib.flk_attend(fake, fake, fake, 1, 0, 128, 128, fake, None, 0, None) \
+        == _lib.FLK_ERR_INVALID_ARGUMENT
+    # empty problems are a no-op success
+    assert lib.flk_qk_prep(fake, fake, fake, fake, fake, 1.0, 0, 64, 2, 128, fake, fake, fake, None) == 0
+    assert lib.flk_attend(fake, fake, fake, 1, 2, 0, 128, fake, None, 0, None) == 0
+    # misaligned pointer
+    odd = ctypes.c_void_p(0x10002)
+    assert lib.flk_attend(odd, fake, fake, 1, 2, 128, 128, fake, None, 0, None) \
+        == _lib.FLK_ERR_INVALID_ARGUMENT
+    # non-finite gain
+    assert lib.flk_qk_prep(fake, fake, fake, fake, fake, float("nan"), 1, 64, 2, 128, fake, fake, fake,
+                           None) == _lib.FLK_ERR_INVALID_ARGUMENT
