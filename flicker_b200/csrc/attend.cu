@@ -7,18 +7,22 @@
 // tensor memory for the whole KV loop and is read exactly once, in the epilogue.
 //
 // One CTA owns two 128-row query tiles of one (batch, head) and walks all KV blocks
-// of 128 rows. Warp roles (320 threads, 1 CTA per SM):
-//   warp 0      TMA producer: Q tiles once, then K_j, V_j into a 4-slot ring of 32 KB slots
-//   warp 1      TMEM allocator + single-thread UMMA issuer
+// of 128 rows. Warp roles (576 threads, 1 CTA per SM):
+//   warp 0      TMA producer: Q tiles once, then K_j, V_j into a 5-slot ring of 32 KB slots
+//   warp 1      TMEM allocator + UMMA issuer
 //   warps 2-5   "softmax" for query tile 0, warps 6-9 for query tile 1: one thread per
 //               query row (TMEM lane), exp + bf16 round + row sum, P written back to TMEM,
 //               then the epilogue O / l -> bf16 -> global.
+// The producer and issuer warps run converged: all 32 lanes walk the loop and wait on the
+// barriers (sleeping try_wait), and lane 0 alone issues the TMA / UMMA / commit instructions
+// through predicated inline PTX.
 // TMEM (512 columns x 128 lanes, fp32): S_t at columns [128t, 128t+128) for t = 0, 1, with
 // P_t (bf16, two per column) written over the first 64 of them; O_t at [256+128t, ...).
 // Per KV block the issuer runs, in order:
 //   PV_0(j) [needs P_0(j)], S_0(j+1), PV_1(j) [needs P_1(j)], S_1(j+1)
-// so one tile's exp overlaps the other tile's two GEMMs. UMMAs from one thread execute
-// in issue order, which is what makes writing S_t(j+1) over P_t(j) safe.
+// so one tile's exp overlaps the other tile's two GEMMs (the fixed order keeps the two tiles
+// half a period apart). UMMAs from one thread execute in issue order, which is what makes
+// writing S_t(j+1) over P_t(j) safe.
 // Shared-memory operands use the 128-byte swizzle written by TMA: Q and K are K-major
 // (head dim contiguous), V is the MN-major B operand of P.V (head dim contiguous).
 // No TMA multicast is used anywhere.
@@ -36,10 +40,11 @@ namespace {
 
 constexpr int kTile = 128;                 // query rows per tile, KV rows per block
 constexpr int kDim = 128;                  // head dim
-constexpr int kSlots = 4;                  // K/V ring slots
+constexpr int kSlots = 4;                  // K/V ring slots (K_j, V_j alternate; 2 blocks of lookahead)
 constexpr int kTileBytes = kTile * kDim * 2;  // 32 KB: one bf16 128 x 128 tile
 constexpr int kHalfBytes = kTileBytes / 2;    // one 64-column TMA box (128 B rows)
-constexpr int kThreads = 320;
+constexpr int kSoftmaxWarps = 8;           // per query tile: 2 per TMEM lane quadrant
+constexpr int kThreads = 32 * (2 + 2 * kSoftmaxWarps);
 constexpr uint32_t kTmemCols = 512;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -51,11 +56,11 @@ struct alignas(1024) Smem {
   uint8_t kv[kSlots][kTileBytes];
   uint64_t q_full;
   uint64_t kv_full[kSlots];
-  uint64_t kv_empty[kSlots];
   uint64_t s_full[2];
-  uint64_t p_full[2];
+  uint64_t p_part[2][2];  // [tile][column chunk]: P chunk c of every softmax warp of the tile is in TMEM
   uint64_t o_full[2];
   uint64_t drain;
+  float l_part[2][2][kTile];  // [tile][column half][row]: row sums of the two halves
   uint32_t tmem_base;
   int abort;
 };
@@ -81,6 +86,37 @@ __device__ __forceinline__ uint64_t desc_mnmajor(const uint8_t* tile, int kc) {
   return umma_desc_sw128(smem_u32(tile) + kc * 2048, kHalfBytes, 1024);
 }
 
+// exp of one 32-column chunk of a row of S -> 16 packed bf16x2 words of P, and the row sum of
+// the bf16-ROUNDED values (kernels.py:124-125 sums fp32(bf16(exp(s)))). One pair in
+// kPolyEvery goes through the FMA-pipe polynomial, the rest through MUFU.EX2, so the SFU is
+// not the only unit producing exponentials.
+constexpr int kPolyEvery = 4;
+__device__ __forceinline__ void exp_chunk(const uint32_t (&r)[32], uint32_t (&pk)[16], float2& l0, float2& l1) {
+  const float2 log2e = make_float2(kLog2e, kLog2e);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float2 x = __fmul2_rn(make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), log2e);
+    float2 e;
+    if (i % kPolyEvery == kPolyEvery - 1) {
+      e = exp2_poly2(x);
+    } else {
+      e.x = ex2_approx(x.x);
+      e.y = ex2_approx(x.y);
+    }
+    pk[i] = pack_bf16x2(e.x, e.y);
+    const float2 rounded = make_float2(__uint_as_float(pk[i] << 16), __uint_as_float(pk[i] & 0xFFFF0000u));
+    if (i & 1)
+      l1 = __fadd2_rn(l1, rounded);
+    else
+      l0 = __fadd2_rn(l0, rounded);
+  }
+}
+
+// TMEM column (within a tile's S region) of the packed P words for KV rows [16kc, 16kc+16):
+// the softmax warp of column half h writes the P of S columns [64h, 64h+64) packed into
+// columns [64h, 64h+32), i.e. over S columns it has already read.
+__device__ __forceinline__ uint32_t p_col(int kc) { return static_cast<uint32_t>((kc >> 2) * 64 + (kc & 3) * 8); }
+
 __global__ void __launch_bounds__(kThreads, 1)
     attend_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const Params p) {
@@ -88,6 +124,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   Smem& sm = *smem_ptr(smem_raw);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const bool leader = lane == 0;  // the one lane of a converged warp that issues TMA / UMMA / commits
 
   const int bh = blockIdx.y;
   const int t0 = blockIdx.x * 2;
@@ -97,13 +134,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
-    for (int s = 0; s < kSlots; ++s) {
-      mbar_init(&sm.kv_full[s], 1);
-      mbar_init(&sm.kv_empty[s], 1);
-    }
+    for (int s = 0; s < kSlots; ++s) mbar_init(&sm.kv_full[s], 1);
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sm.s_full[t], 1);
-      mbar_init(&sm.p_full[t], 128);
+      mbar_init(&sm.p_part[t][0], 32 * kSoftmaxWarps);
+      mbar_init(&sm.p_part[t][1], 32 * kSoftmaxWarps);
       mbar_init(&sm.o_full[t], 1);
     }
     mbar_init(&sm.drain, 1);
@@ -121,8 +156,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort = &sm.abort;
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ TMA producer (whole warp, lane 0 issues)
+    if (leader) {
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
@@ -132,126 +167,141 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(sm.q[t], &tm_q, 0, row, &sm.q_full);
         tma_load_2d(sm.q[t] + kHalfBytes, &tm_q, 64, row, &sm.q_full);
       }
-      int issued[kSlots] = {0, 0, 0, 0};
-      for (int n = 0; n < 2 * n_kv; ++n) {
-        const int slot = n % kSlots;
-        const int use = n / kSlots;
-        if (use > 0 && !mbar_wait(&sm.kv_empty[slot], (use - 1) & 1, abort, p.status)) break;
+    }
+    // Slot reuse needs no barrier of its own: the issuer commits s_full[nt-1] after the last UMMA
+    // of every block, and a commit tracks all earlier UMMAs, so its completion #(b+1) means block
+    // b's P.V (V_b) and the S for block b+1 (K_{b+1}) have run; completion #0 covers S(0) (K_0).
+    // Load n refills the slot of load n-4: K_i (n-4 = 2i) is free after completion #i,
+    // V_i (n-4 = 2i+1) after completion #(i+1).
+    uint64_t* slot_free = &sm.s_full[nt - 1];
+    int issued[kSlots] = {};
+    for (int n = 0; n < 2 * n_kv; ++n) {
+      const int slot = n % kSlots;
+      if (n >= kSlots) {
+        const int m = n - kSlots;
+        const int done = (m & 1) ? (m >> 1) + 1 : (m >> 1);  // completion index of slot_free to await
+        if (!__all_sync(0xffffffffu, mbar_wait(slot_free, done & 1, abort, p.status))) break;
+      }
+      if (leader) {
         mbar_arrive_expect_tx(&sm.kv_full[slot], kTileBytes);
         const void* map = (n & 1) ? static_cast<const void*>(&tm_v) : static_cast<const void*>(&tm_k);
         const int row = row_base + (n >> 1) * kTile;
         tma_load_2d(sm.kv[slot], map, 0, row, &sm.kv_full[slot]);
         tma_load_2d(sm.kv[slot] + kHalfBytes, map, 64, row, &sm.kv_full[slot]);
-        issued[slot] = use + 1;
       }
-      // Never leave with a copy in flight: wait (bounded) for the last fill of every slot.
-      mbar_wait(&sm.q_full, 0, abort, p.status);
-      for (int s = 0; s < kSlots; ++s)
-        if (issued[s] > 0) mbar_wait(&sm.kv_full[s], (issued[s] - 1) & 1, abort, p.status);
+      issued[slot] = n / kSlots + 1;
+      __syncwarp();
     }
+    // Never leave with a copy in flight: wait (bounded) for the last fill of every slot.
+    mbar_wait(&sm.q_full, 0, abort, p.status);
+    for (int s = 0; s < kSlots; ++s)
+      if (issued[s] > 0) mbar_wait(&sm.kv_full[s], (issued[s] - 1) & 1, abort, p.status);
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ------------------------------------------------------------ UMMA issuer
-      bool ok = mbar_wait(&sm.q_full, 0, abort, p.status);
-      tc_fence_after();
-      auto kv_ready = [&](int n) {
-        return mbar_wait(&sm.kv_full[n % kSlots], (n / kSlots) & 1, abort, p.status);
-      };
-      // S_t(0) = Q_t K_0^T
-      if (ok) ok = kv_ready(0);
-      if (ok) {
-        tc_fence_after();
-        const uint8_t* kt = sm.kv[0];
-        for (int t = 0; t < nt; ++t) {
+    // ------------------------------------------------------------ UMMA issuer (whole warp, lane 0 issues)
+    auto wait = [&](uint64_t* bar, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, p.status));
+    };
+    auto kv_ready = [&](int n) { return wait(&sm.kv_full[n % kSlots], (n / kSlots) & 1); };
+    auto qk = [&](int t, const uint8_t* kt) {
 #pragma unroll
-          for (int kc = 0; kc < 8; ++kc)
-            umma_ss(tmem + t * 128, desc_kmajor(sm.q[t], kc), desc_kmajor(kt, kc), kIdescQK, kc > 0);
-          tc_commit(&sm.s_full[t]);
-        }
-        tc_commit(&sm.kv_empty[0]);
+      for (int kc = 0; kc < 8; ++kc)
+        umma_ss_if(leader, tmem + t * 128, desc_kmajor(sm.q[t], kc), desc_kmajor(kt, kc), kIdescQK, kc > 0);
+    };
+    bool ok = wait(&sm.q_full, 0) && kv_ready(0);
+    if (ok) {
+      tc_fence_after();
+      for (int t = 0; t < nt; ++t) {
+        qk(t, sm.kv[0]);  // S_t(0) = Q_t K_0^T
+        tc_commit_if(leader, &sm.s_full[t]);
       }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        const int nv = 2 * j + 1, nk = 2 * j + 2;
-        const bool last = (j == n_kv - 1);
-        ok = kv_ready(nv);
-        if (!ok) break;
-        tc_fence_after();
-        const uint8_t* vt = sm.kv[nv % kSlots];
-        const uint8_t* kt = sm.kv[nk % kSlots];
-        for (int t = 0; t < nt; ++t) {
-          ok = mbar_wait(&sm.p_full[t], j & 1, abort, p.status);
+    }
+    for (int j = 0; ok && j < n_kv; ++j) {
+      const int nv = 2 * j + 1, nk = 2 * j + 2;
+      const bool last = (j == n_kv - 1);
+      ok = kv_ready(nv);
+      if (!ok) break;
+      const uint8_t* vt = sm.kv[nv % kSlots];
+      const uint8_t* kt = sm.kv[nk % kSlots];
+      for (int t = 0; t < nt; ++t) {
+        // P.V in two steps: K-chunks {0,1,4,5} (P chunk 0 of both column halves) as soon as every
+        // softmax warp has written its first chunk, then {2,3,6,7}.
+        for (int c = 0; c < 2 && ok; ++c) {
+          ok = wait(&sm.p_part[t][c], j & 1);
           if (!ok) break;
           tc_fence_after();
 #pragma unroll
-          for (int kc = 0; kc < 8; ++kc)
-            umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kc * 8, desc_mnmajor(vt, kc), kIdescPV,
-                    (j > 0 || kc > 0) ? 1u : 0u);
-          if (last) {
-            tc_commit(&sm.o_full[t]);
-          } else {
-            if (t == 0) {
-              ok = kv_ready(nk);
-              if (!ok) break;
-              tc_fence_after();
-            }
-#pragma unroll
-            for (int kc = 0; kc < 8; ++kc)
-              umma_ss(tmem + t * 128, desc_kmajor(sm.q[t], kc), desc_kmajor(kt, kc), kIdescQK, kc > 0);
-            tc_commit(&sm.s_full[t]);
+          for (int i = 0; i < 4; ++i) {
+            const int kc = (i & 1) + 2 * c + 4 * (i >> 1);  // kv rows [16kc, 16kc+16)
+            umma_ts_if(leader, tmem + 256 + t * 128, tmem + t * 128 + p_col(kc), desc_mnmajor(vt, kc), kIdescPV,
+                       (j > 0 || c > 0 || i > 0) ? 1u : 0u);
           }
         }
         if (!ok) break;
-        tc_commit(&sm.kv_empty[nv % kSlots]);
-        if (!last) tc_commit(&sm.kv_empty[nk % kSlots]);
+        if (last) {
+          tc_commit_if(leader, &sm.o_full[t]);
+          continue;
+        }
+        if (t == 0) {
+          ok = kv_ready(nk);
+          if (!ok) break;
+        }
+        qk(t, kt);  // S_t(j+1) = Q_t K_{j+1}^T, written over P_t(j) after the P.V above has read it
+        tc_commit_if(leader, &sm.s_full[t]);
       }
-      // Drain: every UMMA issued above has completed before TMEM is released.
-      tc_commit(&sm.drain);
-      mbar_wait(&sm.drain, 0, abort, p.status);
+      if (!ok) break;
     }
+    // Drain: every UMMA issued above has completed before TMEM is released.
+    tc_commit_if(leader, &sm.drain);
+    wait(&sm.drain, 0);
   } else {
     // ------------------------------------------------------------ softmax + epilogue
-    const int t = (warp - 2) >> 2;
-    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int sw = warp - 2;                  // softmax warp index 0 .. 2*kSoftmaxWarps-1
+    const int t = sw / kSoftmaxWarps;         // query tile
+    const int half = (sw % kSoftmaxWarps) / 4;  // column half of S / O this warp owns
+    const int quad = warp & 3;                // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
     if (t < nt) {
       const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-      const uint32_t s_addr = tmem + lane_off + t * 128;
-      float l = 0.f;
+      const uint32_t s_addr = tmem + lane_off + t * 128 + half * 64;
+      float2 l0 = make_float2(0.f, 0.f), l1 = make_float2(0.f, 0.f);
       bool ok = true;
       for (int j = 0; j < n_kv; ++j) {
         // Warp-uniform outcome: the tcgen05.ld/st below are .sync.aligned.
         ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_full[t], j & 1, abort, p.status));
         if (!ok) break;
         tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(s_addr + c * 32, r);
-          tmem_wait_ld();
-          uint32_t pk[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float e0 = ex2_approx(__uint_as_float(r[2 * i]) * kLog2e);
-            const float e1 = ex2_approx(__uint_as_float(r[2 * i + 1]) * kLog2e);
-            pk[i] = pack_bf16x2(e0, e1);
-            l += __uint_as_float(pk[i] << 16) + __uint_as_float(pk[i] & 0xFFFF0000u);
-          }
-          tmem_st_32x32b_x16(s_addr + c * 16, pk);
-        }
+        // Two 32-column chunks of this row's half of S; chunk 1 is loading while chunk 0 is
+        // exponentiated, and each chunk's P is handed to the issuer as soon as it is in TMEM.
+        uint32_t ra[32], rb[32], pk[16];
+        tmem_ld_32x32b_x32(s_addr, ra);
+        tmem_wait_ld(ra);
+        tmem_ld_32x32b_x32(s_addr + 32, rb);
+        exp_chunk(ra, pk, l0, l1);
+        tmem_st_32x32b_x16(s_addr, pk);
+        tmem_wait_ld(rb);
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&sm.p_full[t]);
+        mbar_arrive(&sm.p_part[t][0]);
+        exp_chunk(rb, pk, l0, l1);
+        tmem_st_32x32b_x16(s_addr + 16, pk);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&sm.p_part[t][1]);
       }
+      // Row sum over all 128 KV columns: this warp's half plus the other half's partial.
+      sm.l_part[t][half][row] = (l0.x + l0.y) + (l1.x + l1.y);
+      named_barrier_sync(1 + t, 32 * kSoftmaxWarps);
+      const float l = sm.l_part[t][0][row] + sm.l_part[t][1][row];
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.o_full[t], 0, abort, p.status));
       if (ok) {
         tc_fence_after();
-        const uint32_t o_addr = tmem + lane_off + 256 + t * 128;
-        uint16_t* orow = p.o + (static_cast<size_t>(row_base) + (t0 + t) * kTile + row) * kDim;
+        const uint32_t o_addr = tmem + lane_off + 256 + t * 128 + half * 64;
+        uint16_t* orow = p.o + (static_cast<size_t>(row_base) + (t0 + t) * kTile + row) * kDim + half * 64;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(o_addr + c * 32, r);
-          tmem_wait_ld();
+          tmem_wait_ld(r);
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i)
@@ -309,6 +359,7 @@ static bool make_tile_map(CUtensorMap* map, const void* base, long long rows) {
 }
 
 static size_t attend_smem_bytes() { return sizeof(Smem) + 1024; }
+static_assert(sizeof(Smem) + 1024 <= 232448, "attend shared memory exceeds the 227 KB opt-in limit");
 
 int launch_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, uint16_t* o,
                   int* status, cudaStream_t stream) {

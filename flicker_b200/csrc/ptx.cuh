@@ -57,6 +57,21 @@ __device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the phase completes
+// or about kSuspendNs elapse, instead of spinning.
+constexpr uint32_t kSuspendNs = 1000000;
+__device__ __forceinline__ bool mbar_test_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with the given parity has completed. Returns false (after
 // recording the timeout in *status and raising *abort) if it does not within the
 // limit, or if another thread of the CTA or another CTA has already given up.
@@ -65,8 +80,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_test(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t spin = 1; spin < kWaitSpinCap; ++spin) {
-    if (mbar_test(bar, parity)) return true;
-    if ((spin & 255u) == 0) {
+    if (mbar_test_sleep(bar, parity)) return true;
+    {
       if (*abort) return false;
       if (*reinterpret_cast<volatile int*>(status) != 0) {
         *abort = 1;
@@ -78,6 +93,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   *abort = 1;
   atomicExch(status, kErrDeviceTimeout);
   return false;
+}
+
+// Named barrier `id` (1..15) over `count` threads (a multiple of 32).
+__device__ __forceinline__ void named_barrier_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // ---------------------------------------------------------------- TMA
@@ -142,6 +162,38 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
       : "memory");
 }
 
+// Warp-converged forms: every lane of the warp executes the instruction stream and only the
+// lane with `leader` set issues (keeps the issuing warp converged, like elect.sync issue).
+__device__ __forceinline__ void umma_ss_if(bool leader, uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, l;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.ne.b32 l, %5, 0;\n\t"
+      "@l tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(static_cast<uint32_t>(leader))
+      : "memory");
+}
+__device__ __forceinline__ void umma_ts_if(bool leader, uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, l;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "setp.ne.b32 l, %5, 0;\n\t"
+      "@l tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(static_cast<uint32_t>(leader))
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_if(bool leader, uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred l;\n\t"
+      "setp.ne.b32 l, %1, 0;\n\t"
+      "@l tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(
+          smem_u32(bar)),
+      "r"(static_cast<uint32_t>(leader))
+      : "memory");
+}
+
 // UMMA shared-memory matrix descriptor (sm_100 layout): start, leading/stride byte
 // offsets (>> 4), version 1 at bit 46, layout type at bits 61..63 (2 = 128-byte swizzle).
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
@@ -186,6 +238,20 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// tcgen05.wait::ld that also "rewrites" the registers a preceding tcgen05.ld filled, so the
+// compiler cannot schedule any use of them above the wait (the load fills them asynchronously).
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.wait::ld.sync.aligned;"
+      : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+        "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+        "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+        "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+        "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+      :
+      : "memory");
+}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // 2^x on the SFU (MUFU.EX2), flush-to-zero; relative error ~2^-22.
@@ -193,6 +259,25 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x for a pair of floats on the FMA/ALU pipes (no SFU): x = n + f with n = rint(x),
+// f in [-1/2, 1/2]; 2^f from a degree-4 minimax polynomial (relative error 3.6e-6, derived by
+// csrc/exp2_poly.py), and 2^n applied by adding n to the exponent field. Valid for
+// -126 <= x < 128 (the bounded-logit domain: |x| <= 80 * log2(e) < 116).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23: x + kRound rounds x to an integer in the low bits
+  const float2 u = __fadd2_rn(x, make_float2(kRound, kRound));
+  const float2 n = __fadd2_rn(u, make_float2(-kRound, -kRound));
+  const float2 f = __ffma2_rn(n, make_float2(-1.0f, -1.0f), x);
+  float2 p = __ffma2_rn(f, make_float2(0.009782912209630013f, 0.009782912209630013f),
+                        make_float2(0.055976882576942444f, 0.055976882576942444f));
+  p = __ffma2_rn(p, f, make_float2(0.24020710587501526f, 0.24020710587501526f));
+  p = __ffma2_rn(p, f, make_float2(0.6931136250495911f, 0.6931136250495911f));
+  p = __ffma2_rn(p, f, make_float2(1.0f, 1.0f));
+  // The low bits of u hold n (two's complement, offset by 1.5 * 2^23 whose bits vanish in the shift).
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(u.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(u.y) << 23)));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
 
 #include "flicker_b200.h"
 
@@ -28,7 +29,6 @@ namespace flk {
 namespace {
 
 constexpr int kHeadDim = 128;
-constexpr int kRowsPerItem = 8;
 constexpr int kThreads = 256;
 
 __device__ __forceinline__ uint4 ld_stream(const uint16_t* p) {
@@ -39,19 +39,46 @@ __device__ __forceinline__ uint4 ld_stream(const uint16_t* p) {
   return r;
 }
 
-__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
-__device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+// bf16 pair word (low half = even column) -> the two values as fp32.
+__device__ __forceinline__ float2 unpack(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+}
+__device__ __forceinline__ uint32_t pack(float2 v) {
+  __nv_bfloat162 b = __float22bfloat162_rn(v);
+  return *reinterpret_cast<uint32_t*>(&b);
+}
+__device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t w) { return *reinterpret_cast<__nv_bfloat162*>(&w); }
+__device__ __forceinline__ uint32_t as_u32(__nv_bfloat162 b) { return *reinterpret_cast<uint32_t*>(&b); }
 
-__global__ void __launch_bounds__(kThreads) qk_prep_kernel(const uint16_t* __restrict__ qkv,
-                                                           const uint16_t* __restrict__ q_scale,
-                                                           const uint16_t* __restrict__ k_scale,
-                                                           const float* __restrict__ cos_t,
-                                                           const float* __restrict__ sin_t, float q_gain,
-                                                           int L, int H, int groups, long long n_items,
-                                                           uint16_t* __restrict__ q_out,
-                                                           uint16_t* __restrict__ k_out,
-                                                           uint16_t* __restrict__ v_out) {
+// One row of 8 columns (4 pair words) owned by this lane: RMSNorm -> bf16 -> * scale (bf16) ->
+// RoPE in fp32 -> (* gain) -> bf16. `ss` is the row's sum of squares (all 128 columns).
+__device__ __forceinline__ uint4 norm_rope(uint4 x, float ss, uint4 scale, const float2 (&c)[4],
+                                           const float2 (&sn)[4], float gain) {
+  // rsqrt(mean + eps) as the correctly rounded reciprocal of the correctly rounded sqrt.
+  const float inv = __frcp_rn(__fsqrt_rn(ss * (1.0f / kHeadDim) + 1e-6f));
+  const float2 inv2 = make_float2(inv, inv);
+  const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
+  const uint32_t sw[4] = {scale.x, scale.y, scale.z, scale.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    // bf16(x * inv), then the bf16 x bf16 scale multiply rounded to bf16 (exact product, one rounding).
+    const __nv_bfloat162 nb = __hmul2(__float22bfloat162_rn(__fmul2_rn(unpack(xw[j]), inv2)), as_bf2(sw[j]));
+    const float2 w = unpack(as_u32(nb));
+    // rotation c * w + s * swap(w) with separate roundings (no contraction), as the reference body.
+    float2 r = __fadd2_rn(__fmul2_rn(c[j], w), __fmul2_rn(sn[j], make_float2(w.y, w.x)));
+    if (gain != 1.0f) r = __fmul2_rn(r, make_float2(gain, gain));
+    o[j] = pack(r);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+template <int kRows, int kMinBlocks>
+__global__ void __launch_bounds__(kThreads, kMinBlocks)
+    qk_prep_kernel(const uint16_t* __restrict__ qkv, const uint16_t* __restrict__ q_scale,
+                   const uint16_t* __restrict__ k_scale, const float* __restrict__ cos_t,
+                   const float* __restrict__ sin_t, float q_gain, int L, int H, int groups, long long n_items,
+                   uint16_t* __restrict__ q_out, uint16_t* __restrict__ k_out, uint16_t* __restrict__ v_out) {
   const long long item = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 4;
   const int lane16 = threadIdx.x & 15;
   const bool valid = item < n_items;
@@ -64,37 +91,37 @@ __global__ void __launch_bounds__(kThreads) qk_prep_kernel(const uint16_t* __res
   const int col = lane16 * 8;
 
   // Issue the row loads first (independent of everything else).
-  uint4 x[kRowsPerItem];
+  uint4 x[kRows];
   const uint16_t* src = qkv + (static_cast<size_t>(token) * rows3) * kHeadDim + col;
 #pragma unroll
-  for (int i = 0; i < kRowsPerItem; ++i) {
-    const int r = g * kRowsPerItem + i;
+  for (int i = 0; i < kRows; ++i) {
+    const int r = g * kRows + i;
     x[i] = (valid && r < rows3) ? ld_stream(src + static_cast<size_t>(r) * kHeadDim) : make_uint4(0, 0, 0, 0);
   }
 
   const float4* cp = reinterpret_cast<const float4*>(cos_t + static_cast<size_t>(l) * kHeadDim + col);
   const float4* sp = reinterpret_cast<const float4*>(sin_t + static_cast<size_t>(l) * kHeadDim + col);
   const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
-  const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-  const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+  const float2 cs[4] = {make_float2(c0.x, c0.y), make_float2(c0.z, c0.w), make_float2(c1.x, c1.y),
+                        make_float2(c1.z, c1.w)};
+  const float2 sn[4] = {make_float2(s0.x, s0.y), make_float2(s0.z, s0.w), make_float2(s1.x, s1.y),
+                        make_float2(s1.z, s1.w)};
   const uint4 qsv = __ldg(reinterpret_cast<const uint4*>(q_scale + col));
   const uint4 ksv = __ldg(reinterpret_cast<const uint4*>(k_scale + col));
 
 #pragma unroll
-  for (int i = 0; i < kRowsPerItem; ++i) {
-    const int r = g * kRowsPerItem + i;
+  for (int i = 0; i < kRows; ++i) {
+    const int r = g * kRows + i;
     const int kind = r < H ? 0 : (r < 2 * H ? 1 : 2);  // uniform across the half-warp
     const int h = r - kind * H;
+    float2 s2 = make_float2(0.f, 0.f);
     const uint32_t w[4] = {x[i].x, x[i].y, x[i].z, x[i].w};
-    float f[8];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      f[2 * j] = bf_lo(w[j]);
-      f[2 * j + 1] = bf_hi(w[j]);
+      const float2 f = unpack(w[j]);
+      s2 = __ffma2_rn(f, f, s2);  // squares of bf16 values are exact in fp32
     }
-    float ss = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+    float ss = s2.x + s2.y;
     ss += __shfl_xor_sync(0xffffffffu, ss, 8, 16);
     ss += __shfl_xor_sync(0xffffffffu, ss, 4, 16);
     ss += __shfl_xor_sync(0xffffffffu, ss, 2, 16);
@@ -106,48 +133,46 @@ __global__ void __launch_bounds__(kThreads) qk_prep_kernel(const uint16_t* __res
       *reinterpret_cast<uint4*>(v_out + dst) = x[i];
       continue;
     }
-    // rsqrt(mean + eps) as 1 / sqrt(.) with IEEE rounding of each step.
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(ss * (1.0f / kHeadDim) + 1e-6f));
-    const uint4 sv = kind == 0 ? qsv : ksv;
-    const uint32_t sw[4] = {sv.x, sv.y, sv.z, sv.w};
-    float n[8];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      n[2 * j] = round_bf16(__fmul_rn(round_bf16(__fmul_rn(f[2 * j], inv)), bf_lo(sw[j])));
-      n[2 * j + 1] = round_bf16(__fmul_rn(round_bf16(__fmul_rn(f[2 * j + 1], inv)), bf_hi(sw[j])));
-    }
-    const float gain = kind == 0 ? q_gain : 1.0f;
-    uint32_t o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int e = 2 * j, d = 2 * j + 1;
-      float re = __fadd_rn(__fmul_rn(cs[e], n[e]), __fmul_rn(sn[e], n[d]));
-      float rd = __fadd_rn(__fmul_rn(cs[d], n[d]), __fmul_rn(sn[d], n[e]));
-      if (gain != 1.0f) {
-        re = __fmul_rn(gain, re);
-        rd = __fmul_rn(gain, rd);
-      }
-      __nv_bfloat162 pr = __floats2bfloat162_rn(re, rd);
-      o[j] = *reinterpret_cast<uint32_t*>(&pr);
-    }
-    uint16_t* out = kind == 0 ? q_out : k_out;
-    *reinterpret_cast<uint4*>(out + dst) = make_uint4(o[0], o[1], o[2], o[3]);
+    const uint4 o = norm_rope(x[i], ss, kind == 0 ? qsv : ksv, cs, sn, kind == 0 ? q_gain : 1.0f);
+    *reinterpret_cast<uint4*>((kind == 0 ? q_out : k_out) + dst) = o;
   }
 }
 
 }  // namespace
 
+template <int kRows, int kMinBlocks>
+static int launch_rows(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t* k_scale, const float* cos_t,
+                       const float* sin_t, float q_gain, int B, int L, int H, uint16_t* q, uint16_t* k, uint16_t* v,
+                       cudaStream_t stream) {
+  const int groups = (3 * H + kRows - 1) / kRows;
+  const long long n_items = static_cast<long long>(B) * L * groups;
+  const long long blocks = (n_items * 16 + kThreads - 1) / kThreads;
+  if (blocks > 0x7FFFFFFFLL) return FLK_ERR_UNSUPPORTED;
+  qk_prep_kernel<kRows, kMinBlocks><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
+      qkv, q_scale, k_scale, cos_t, sin_t, q_gain, L, H, groups, n_items, q, k, v);
+  return cudaGetLastError() == cudaSuccess ? FLK_OK : FLK_ERR_CUDA;
+}
+
+// Tuning sweep only: FLK_QK_PREP_VARIANT picks rows per work item / occupancy (read once).
+static int qk_prep_variant() {
+  static const int v = [] {
+    const char* e = getenv("FLK_QK_PREP_VARIANT");
+    return e ? atoi(e) : 0;
+  }();
+  return v;
+}
+
 int launch_qk_prep(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t* k_scale, const float* cos_t,
                    const float* sin_t, float q_gain, int B, int L, int H, uint16_t* q, uint16_t* k, uint16_t* v,
                    cudaStream_t stream) {
-  const int groups = (3 * H + kRowsPerItem - 1) / kRowsPerItem;
-  const long long n_items = static_cast<long long>(B) * L * groups;
-  const long long threads = n_items * 16;
-  const long long blocks = (threads + kThreads - 1) / kThreads;
-  if (blocks > 0x7FFFFFFFLL) return FLK_ERR_UNSUPPORTED;
-  qk_prep_kernel<<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
-      qkv, q_scale, k_scale, cos_t, sin_t, q_gain, L, H, groups, n_items, q, k, v);
-  return cudaGetLastError() == cudaSuccess ? FLK_OK : FLK_ERR_CUDA;
+  switch (qk_prep_variant()) {
+    case 1: return launch_rows<8, 2>(qkv, q_scale, k_scale, cos_t, sin_t, q_gain, B, L, H, q, k, v, stream);
+    case 2: return launch_rows<8, 3>(qkv, q_scale, k_scale, cos_t, sin_t, q_gain, B, L, H, q, k, v, stream);
+    case 3: return launch_rows<4, 4>(qkv, q_scale, k_scale, cos_t, sin_t, q_gain, B, L, H, q, k, v, stream);
+    case 4: return launch_rows<4, 6>(qkv, q_scale, k_scale, cos_t, sin_t, q_gain, B, L, H, q, k, v, stream);
+    case 5: return launch_rows<6, 4>(qkv, q_scale, k_scale, cos_t, sin_t, q_gain, B, L, H, q, k, v, stream);
+    default: return launch_rows<8, 3>(qkv, q_scale, k_scale, cos_t, sin_t, q_gain, B, L, H, q, k, v, stream);
+  }
 }
 
 }  // namespace flk

@@ -35,11 +35,11 @@ def test_golden(name, gain_key):
     # Only the fp32 sum-of-squares order differs from the reference body: near bit-exact.
     assert bit_equal_fraction(q, g[gain_key]) > 0.995
     assert bit_equal_fraction(k, g["k"]) > 0.995
-    assert R.within_tolerance(q, g[gain_key].astype(np.float32))
-    assert R.within_tolerance(k, g["k"].astype(np.float32))
+    assert R.within_tolerance_scaled(q, g[gain_key].astype(np.float32))
+    assert R.within_tolerance_scaled(k, g["k"].astype(np.float32))
     # ... and the plain-XLA path of the reference (gain folded into q).
-    assert R.within_tolerance(q, g["q_xla"].astype(np.float32) * gain)
-    assert R.within_tolerance(k, g["k_xla"].astype(np.float32))
+    assert R.within_tolerance_scaled(q, g["q_xla"].astype(np.float32) * gain)
+    assert R.within_tolerance_scaled(k, g["k_xla"].astype(np.float32))
 
 
 @pytest.mark.parametrize("config", ["512", "1024"])
@@ -49,11 +49,11 @@ def test_config_full_size(config):
     wq, wk, wv = R.qk_prep_kernel(qkv, qs, ks, freqs, R.NUM_HEADS)
     assert bit_equal_fraction(v, wv) == 1.0
     assert bit_equal_fraction(q, wq) > 0.995 and bit_equal_fraction(k, wk) > 0.995
-    assert R.within_tolerance(q, wq.astype(np.float32))
-    assert R.within_tolerance(k, wk.astype(np.float32))
+    assert R.within_tolerance_scaled(q, wq.astype(np.float32))
+    assert R.within_tolerance_scaled(k, wk.astype(np.float32))
     xq, xk, _ = R.qkv_prep_xla(qkv, qs, ks, pe, R.NUM_HEADS)
-    assert R.within_tolerance(q, xq.astype(np.float32) * freqs.q_gain)
-    assert R.within_tolerance(k, xk.astype(np.float32))
+    assert R.within_tolerance_scaled(q, xq.astype(np.float32) * freqs.q_gain)
+    assert R.within_tolerance_scaled(k, xk.astype(np.float32))
 
 
 def test_batch8_seeds_independent():
@@ -90,7 +90,7 @@ def test_ragged_shapes_through_c_abi(B, L, H):
     for got, w in zip(outs, want):
         got = to_host(got)
         assert bit_equal_fraction(got, w) > 0.99
-        assert R.within_tolerance(got, w.astype(np.float32))
+        assert R.within_tolerance_scaled(got, w.astype(np.float32))
 
 
 def test_deterministic_and_stream_ordered():
