@@ -29,6 +29,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 
 #include "flicker_b200.h"
@@ -66,10 +67,13 @@ struct alignas(1024) Smem {
 };
 
 struct Params {
-  int S;         // sequence length (multiple of 128)
-  int n_tiles;   // S / 128
-  uint16_t* o;   // [B*H*S, 128] bf16
-  int* status;   // device status word
+  int S;          // sequence length (multiple of 128)
+  int n_tiles;    // S / 128
+  int n_splits;   // KV splits (gridDim.z); 1 = the CTA normalises and writes o itself
+  uint16_t* o;    // [B*H*S, 128] bf16
+  float* acc;     // split > 1: [n_splits, B*H*S, 128] fp32 un-normalised partial P.V
+  float* lsum;    // split > 1: [n_splits, B*H*S] fp32 partial row sums
+  int* status;    // device status word
 };
 
 __device__ __forceinline__ Smem* smem_ptr(uint8_t* raw) {
@@ -129,7 +133,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int bh = blockIdx.y;
   const int t0 = blockIdx.x * 2;
   const int nt = min(2, p.n_tiles - t0);
-  const int n_kv = p.n_tiles;
+  // KV blocks [kv0, kv0 + n_kv) of this split. Without a running max the splits' (acc, l) simply add.
+  const int split = blockIdx.z;
+  const int kv0 = static_cast<int>(static_cast<long long>(p.n_tiles) * split / p.n_splits);
+  const int n_kv = static_cast<int>(static_cast<long long>(p.n_tiles) * (split + 1) / p.n_splits) - kv0;
   const int row_base = bh * p.S;
 
   if (threadIdx.x == 0) {
@@ -185,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (leader) {
         mbar_arrive_expect_tx(&sm.kv_full[slot], kTileBytes);
         const void* map = (n & 1) ? static_cast<const void*>(&tm_v) : static_cast<const void*>(&tm_k);
-        const int row = row_base + (n >> 1) * kTile;
+        const int row = row_base + (kv0 + (n >> 1)) * kTile;
         tma_load_2d(sm.kv[slot], map, 0, row, &sm.kv_full[slot]);
         tma_load_2d(sm.kv[slot] + kHalfBytes, map, 64, row, &sm.kv_full[slot]);
       }
@@ -296,20 +303,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) {
         tc_fence_after();
         const uint32_t o_addr = tmem + lane_off + 256 + t * 128 + half * 64;
-        uint16_t* orow = p.o + (static_cast<size_t>(row_base) + (t0 + t) * kTile + row) * kDim + half * 64;
+        const size_t grow = static_cast<size_t>(row_base) + (t0 + t) * kTile + row;  // global query row
+        if (p.n_splits == 1) {
+          uint16_t* orow = p.o + grow * kDim + half * 64;
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(o_addr + c * 32, r);
-          tmem_wait_ld(r);
-          uint32_t pk[16];
+          for (int c = 0; c < 2; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(o_addr + c * 32, r);
+            tmem_wait_ld(r);
+            uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            pk[i] = pack_bf16x2(__fdiv_rn(__uint_as_float(r[2 * i]), l),
-                                __fdiv_rn(__uint_as_float(r[2 * i + 1]), l));
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+            for (int i = 0; i < 16; ++i)
+              pk[i] = pack_bf16x2(__fdiv_rn(__uint_as_float(r[2 * i]), l),
+                                  __fdiv_rn(__uint_as_float(r[2 * i + 1]), l));
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+          }
+        } else {
+          // Partial result of this split: un-normalised fp32 accumulator and row sum.
+          const size_t plane = static_cast<size_t>(gridDim.y) * p.S;  // rows per split
+          float* arow = p.acc + (split * plane + grow) * kDim + half * 64;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(o_addr + c * 32, r);
+            tmem_wait_ld(r);
+            uint4* dst = reinterpret_cast<uint4*>(arow + c * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dst[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+          }
+          if (half == 0) p.lsum[split * plane + grow] = l;
         }
       }
     }
@@ -321,6 +345,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
+}
+
+// o = bf16(sum_s acc_s / sum_s l_s) over the KV splits; one thread per 8 output columns.
+__global__ void __launch_bounds__(256) combine_splits_kernel(const float* __restrict__ acc,
+                                                             const float* __restrict__ lsum, int n_splits,
+                                                             long long rows, uint16_t* __restrict__ o) {
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= rows * (kDim / 8)) return;
+  const long long row = idx / (kDim / 8);
+  const int col = static_cast<int>(idx % (kDim / 8)) * 8;
+  float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float l = 0.f;
+  for (int s = 0; s < n_splits; ++s) {
+    const float4* src = reinterpret_cast<const float4*>(acc + (s * rows + row) * kDim + col);
+    const float4 x = src[0], y = src[1];
+    a[0] += x.x; a[1] += x.y; a[2] += x.z; a[3] += x.w;
+    a[4] += y.x; a[5] += y.y; a[6] += y.z; a[7] += y.w;
+    l += lsum[s * rows + row];
+  }
+  uint32_t pk[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) pk[i] = pack_bf16x2(__fdiv_rn(a[2 * i], l), __fdiv_rn(a[2 * i + 1], l));
+  *reinterpret_cast<uint4*>(o + row * kDim + col) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
 }
 
 }  // namespace
@@ -361,8 +408,23 @@ static bool make_tile_map(CUtensorMap* map, const void* base, long long rows) {
 static size_t attend_smem_bytes() { return sizeof(Smem) + 1024; }
 static_assert(sizeof(Smem) + 1024 <= 232448, "attend shared memory exceeds the 227 KB opt-in limit");
 
+// KV splits for a shape on a device with `sms` SMs: enough CTAs to fill one wave of SMs
+// when (batch x heads x query-tile pairs) alone would leave most of them idle.
+int attend_splits(int B, int H, int S, int sms) {
+  const long long ctas = static_cast<long long>(B) * H * ((S / kTile + 1) / 2);
+  if (ctas <= 0 || ctas * 2 > sms) return 1;
+  const int n_kv = S / kTile;
+  return static_cast<int>(std::min<long long>(n_kv, std::max<long long>(1, sms / ctas)));
+}
+
+size_t attend_workspace_bytes(int B, int H, int S, int splits) {
+  if (splits <= 1) return 0;
+  const size_t rows = static_cast<size_t>(B) * H * S;
+  return splits * rows * (kDim + 1) * sizeof(float);
+}
+
 int launch_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, uint16_t* o,
-                  int* status, cudaStream_t stream) {
+                  int splits, void* workspace, int* status, cudaStream_t stream) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return FLK_ERR_CUDA;
   static bool configured[64] = {};
@@ -380,11 +442,21 @@ int launch_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B
   Params p;
   p.S = S;
   p.n_tiles = S / kTile;
+  p.n_splits = splits;
   p.o = o;
+  p.acc = splits > 1 ? static_cast<float*>(workspace) : nullptr;
+  p.lsum = splits > 1 ? p.acc + static_cast<size_t>(splits) * rows * kDim : nullptr;
   p.status = status;
-  const dim3 grid((p.n_tiles + 1) / 2, B * H);
+  const dim3 grid((p.n_tiles + 1) / 2, B * H, splits);
   attend_kernel<<<grid, kThreads, attend_smem_bytes(), stream>>>(mq, mk, mv, p);
-  return cudaGetLastError() == cudaSuccess ? FLK_OK : FLK_ERR_CUDA;
+  if (cudaGetLastError() != cudaSuccess) return FLK_ERR_CUDA;
+  if (splits > 1) {
+    const long long threads = rows * (kDim / 8);
+    combine_splits_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(p.acc, p.lsum, splits,
+                                                                                              rows, o);
+    if (cudaGetLastError() != cudaSuccess) return FLK_ERR_CUDA;
+  }
+  return FLK_OK;
 }
 
 }  // namespace flk

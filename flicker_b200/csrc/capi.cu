@@ -17,7 +17,9 @@ int launch_qk_prep(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t*
                    const float* sin_t, float q_gain, int B, int L, int H, uint16_t* q, uint16_t* k, uint16_t* v,
                    cudaStream_t stream);
 int launch_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, uint16_t* o,
-                  int* status, cudaStream_t stream);
+                  int splits, void* workspace, int* status, cudaStream_t stream);
+int attend_splits(int B, int H, int S, int sms);
+size_t attend_workspace_bytes(int B, int H, int S, int splits);
 }  // namespace flk
 
 // Device status word: 0, or FLK_ERR_DEVICE_TIMEOUT after a bounded in-kernel wait ran out.
@@ -31,6 +33,7 @@ constexpr float kExpLimit = 80.0f;  // src/flicker/kernels.py:95
 struct DeviceState {
   bool ready = false;
   bool is_sm100 = false;
+  int sms = 0;            // streaming multiprocessors
   int* status = nullptr;  // device address of g_flk_status on this device
 };
 
@@ -55,6 +58,10 @@ const DeviceState* device_state(int* err) {
       return nullptr;
     }
     st.is_sm100 = (major == 10 && minor == 0);
+    if (cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      *err = FLK_ERR_CUDA;
+      return nullptr;
+    }
     void* addr = nullptr;
     if (st.is_sm100 && cudaGetSymbolAddress(&addr, g_flk_status) != cudaSuccess) {
       *err = FLK_ERR_CUDA;
@@ -71,6 +78,26 @@ const DeviceState* device_state(int* err) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool attend_shape_ok(int B, int H, int S, int D, int* err) {
+  if (B < 0 || H <= 0 || S < 0) {
+    *err = FLK_ERR_INVALID_ARGUMENT;
+    return false;
+  }
+  if (D != 128) {
+    *err = FLK_ERR_UNSUPPORTED;
+    return false;
+  }
+  if (S % 128 != 0) {
+    *err = FLK_ERR_INVALID_ARGUMENT;
+    return false;
+  }
+  if (static_cast<long long>(B) * H > 65535 || static_cast<long long>(B) * H * S > 0x7FFFFFFFLL) {
+    *err = FLK_ERR_UNSUPPORTED;
+    return false;
+  }
+  return true;
+}
 
 }  // namespace
 
@@ -108,30 +135,35 @@ int flk_qk_prep(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t* k_
 }
 
 size_t flk_attend_workspace_size(int B, int H, int S, int D) {
-  (void)B;
-  (void)H;
-  (void)S;
-  (void)D;
-  return 0;
+  int err = FLK_OK;
+  if (!attend_shape_ok(B, H, S, D, &err) || static_cast<long long>(B) * S == 0) return 0;
+  const DeviceState* st = device_state(&err);
+  if (!st) return 0;
+  return flk::attend_workspace_bytes(B, H, S, flk::attend_splits(B, H, S, st->sms));
 }
 
 int flk_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, int D, uint16_t* o,
                void* workspace, size_t ws_bytes, void* stream) {
-  (void)workspace;
-  (void)ws_bytes;
-  if (B < 0 || H <= 0 || S < 0) return FLK_ERR_INVALID_ARGUMENT;
-  if (D != 128) return FLK_ERR_UNSUPPORTED;
-  if (S % 128 != 0) return FLK_ERR_INVALID_ARGUMENT;
+  int err = FLK_OK;
+  if (!attend_shape_ok(B, H, S, D, &err)) return err;
   if (static_cast<long long>(B) * S == 0) return FLK_OK;
-  if (static_cast<long long>(B) * H > 65535 || static_cast<long long>(B) * H * S > 0x7FFFFFFFLL)
-    return FLK_ERR_UNSUPPORTED;
   const void* ptrs[] = {q, k, v, o};
   for (const void* p : ptrs)
     if (p == nullptr || !aligned16(p)) return FLK_ERR_INVALID_ARGUMENT;
-  int err = FLK_OK;
   const DeviceState* st = device_state(&err);
   if (!st) return err;
-  return flk::launch_attend(q, k, v, B, H, S, o, st->status, static_cast<cudaStream_t>(stream));
+  // Low-occupancy shapes run split over KV when the caller provides the workspace; a caller
+  // that passes no workspace (NULL, 0 bytes) gets the unsplit kernel.
+  int splits = flk::attend_splits(B, H, S, st->sms);
+  if (splits > 1) {
+    const size_t need = flk::attend_workspace_bytes(B, H, S, splits);
+    if (workspace == nullptr && ws_bytes == 0) {
+      splits = 1;
+    } else if (workspace == nullptr || ws_bytes < need || !aligned16(workspace)) {
+      return FLK_ERR_WORKSPACE;
+    }
+  }
+  return flk::launch_attend(q, k, v, B, H, S, o, splits, workspace, st->status, static_cast<cudaStream_t>(stream));
 }
 
 int flk_logit_bound(const float* q_scale, const float* k_scale, int D, float* bound) {
