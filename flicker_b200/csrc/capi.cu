@@ -101,6 +101,15 @@ bool attend_shape_ok(int B, int H, int S, int D, int* err) {
 
 }  // namespace
 
+namespace flk {
+// Device address of the status word on the current device (set up on first use), or nullptr
+// with *err set. Lets other translation units of the library hand it to their kernels.
+int* current_device_status(int* err) {
+  const DeviceState* st = device_state(err);
+  return st ? st->status : nullptr;
+}
+}  // namespace flk
+
 extern "C" {
 
 int flk_abi_version(void) { return 100; }

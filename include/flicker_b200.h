@@ -69,6 +69,18 @@ int flk_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v,
 size_t flk_attend_workspace_size(int B, int H, int S, int D);
 
 /*
+ * flk_attend for callers that cannot allocate device memory. No counterpart in the reference.
+ * Same arguments and result as flk_attend minus the workspace: when the shape runs split over
+ * KV, the partial results go to a 16 MiB scratch array built into the library (held on every
+ * GPU that loads it) instead of caller memory, so the call allocates nothing. Shapes needing
+ * more than 16 MiB of split scratch return FLK_ERR_WORKSPACE. The first call on a device sets
+ * up the scratch address (make it before any stream capture); calls share the scratch, so
+ * calls whose kernels overlap on the GPU race and must be ordered by the caller.
+ */
+int flk_attend_noalloc(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                       int B, int H, int S, int D, uint16_t* o, void* stream);
+
+/*
  * Load-time guard of the max-free softmax. Replaces kernels.logit_bound
  * (src/flicker/kernels.py:99-101) and the refusal in loader.check_logit_bound
  * (src/flicker/loader.py:115-128): returns sqrt(D) * max|q_scale| * max|k_scale|
