@@ -11,16 +11,16 @@
 //   * the RoPE partner of column 2i is column 2i+1 of the same lane (no shuffle);
 //   * the cos/sin lane tables and both scale vectors are loaded once per item and reused
 //     for its 8 rows (they are L2-resident: 1 KB per token);
-//   * the sum of squares is reduced across the 16 lanes with 4 xor-shuffles;
+//   * the sum of squares is reduced across the 16 lanes with 4 xor-shuffles (q/k rows only;
+//     v rows are copied straight through);
 //   * all 8 row loads of an item are issued before any math (8 x 16 B in flight per lane).
-// Rounding follows the reference body exactly: fp32 norm, bf16 round, bf16 x bf16 scale
-// multiply rounded to bf16, fp32 rotation c*w + s*swap (no FMA contraction), q gain in
+// Rounding follows the reference body: fp32 norm (rsqrt on the SFU), bf16 round, bf16 x bf16
+// scale multiply rounded to bf16, fp32 rotation c*w + s*swap (no FMA contraction), q gain in
 // fp32, final bf16 round.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
-#include <cstdlib>
 
 #include "flicker_b200.h"
 
@@ -54,8 +54,8 @@ __device__ __forceinline__ uint32_t as_u32(__nv_bfloat162 b) { return *reinterpr
 // RoPE in fp32 -> (* gain) -> bf16. `ss` is the row's sum of squares (all 128 columns).
 __device__ __forceinline__ uint4 norm_rope(uint4 x, float ss, uint4 scale, const float2 (&c)[4],
                                            const float2 (&sn)[4], float gain) {
-  // rsqrt(mean + eps) as the correctly rounded reciprocal of the correctly rounded sqrt.
-  const float inv = __frcp_rn(__fsqrt_rn(ss * (1.0f / kHeadDim) + 1e-6f));
+  // rsqrt(mean + eps) on the SFU (<= 2 ulp; lax.rsqrt's own ulps are not pinned by the reference).
+  const float inv = rsqrtf(ss * (1.0f / kHeadDim) + 1e-6f);
   const float2 inv2 = make_float2(inv, inv);
   const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
   const uint32_t sw[4] = {scale.x, scale.y, scale.z, scale.w};
@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
   const long long item = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 4;
   const int lane16 = threadIdx.x & 15;
   const bool valid = item < n_items;
-  const long long it = valid ? item : 0;  // keep every lane in the shuffles below
+  const long long it = valid ? item : 0;  // clamped so the index math below stays in range
   const long long token = it / groups;    // b * L + l
   const int g = static_cast<int>(it - token * groups);
   const int l = static_cast<int>(token % L);
@@ -114,6 +114,12 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
     const int r = g * kRows + i;
     const int kind = r < H ? 0 : (r < 2 * H ? 1 : 2);  // uniform across the half-warp
     const int h = r - kind * H;
+    if (!valid || r >= rows3) continue;
+    const size_t dst = ((static_cast<size_t>(b) * H + h) * L + l) * kHeadDim + col;
+    if (kind == 2) {  // v rows are copied straight through
+      *reinterpret_cast<uint4*>(v_out + dst) = x[i];
+      continue;
+    }
     float2 s2 = make_float2(0.f, 0.f);
     const uint32_t w[4] = {x[i].x, x[i].y, x[i].z, x[i].w};
 #pragma unroll
@@ -121,18 +127,13 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
       const float2 f = unpack(w[j]);
       s2 = __ffma2_rn(f, f, s2);  // squares of bf16 values are exact in fp32
     }
+    // Sum over this half-warp's 16 lanes (the two half-warps of a warp decide independently).
+    const unsigned hmask = 0xFFFFu << (threadIdx.x & 16);
     float ss = s2.x + s2.y;
-    ss += __shfl_xor_sync(0xffffffffu, ss, 8, 16);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 4, 16);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 2, 16);
-    ss += __shfl_xor_sync(0xffffffffu, ss, 1, 16);
-    if (!valid || r >= rows3) continue;
-
-    const size_t dst = ((static_cast<size_t>(b) * H + h) * L + l) * kHeadDim + col;
-    if (kind == 2) {
-      *reinterpret_cast<uint4*>(v_out + dst) = x[i];
-      continue;
-    }
+    ss += __shfl_xor_sync(hmask, ss, 8, 16);
+    ss += __shfl_xor_sync(hmask, ss, 4, 16);
+    ss += __shfl_xor_sync(hmask, ss, 2, 16);
+    ss += __shfl_xor_sync(hmask, ss, 1, 16);
     const uint4 o = norm_rope(x[i], ss, kind == 0 ? qsv : ksv, cs, sn, kind == 0 ? q_gain : 1.0f);
     *reinterpret_cast<uint4*>((kind == 0 ? q_out : k_out) + dst) = o;
   }
@@ -153,26 +154,12 @@ static int launch_rows(const uint16_t* qkv, const uint16_t* q_scale, const uint1
   return cudaGetLastError() == cudaSuccess ? FLK_OK : FLK_ERR_CUDA;
 }
 
-// Tuning sweep only: FLK_QK_PREP_VARIANT picks rows per work item / occupancy (read once).
-static int qk_prep_variant() {
-  static const int v = [] {
-    const char* e = getenv("FLK_QK_PREP_VARIANT");
-    return e ? atoi(e) : 0;
-  }();
-  return v;
-}
-
 int launch_qk_prep(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t* k_scale, const float* cos_t,
                    const float* sin_t, float q_gain, int B, int L, int H, uint16_t* q, uint16_t* k, uint16_t* v,
                    cudaStream_t stream) {
-  switch (qk_prep_variant()) {
-    case 1: return launch_rows<8, 2>(qkv, q_scale, k_scale, cos_t, sin_t, q_gain, B, L, H, q, k, v, stream);
-    case 2: return launch_rows<8, 3>(qkv, q_scale, k_scale, cos_t, sin_t, q_gain, B, L, H, q, k, v, stream);
-    case 3: return launch_rows<4, 4>(qkv, q_scale, k_scale, cos_t, sin_t, q_gain, B, L, H, q, k, v, stream);
-    case 4: return launch_rows<4, 6>(qkv, q_scale, k_scale, cos_t, sin_t, q_gain, B, L, H, q, k, v, stream);
-    case 5: return launch_rows<6, 4>(qkv, q_scale, k_scale, cos_t, sin_t, q_gain, B, L, H, q, k, v, stream);
-    default: return launch_rows<8, 3>(qkv, q_scale, k_scale, cos_t, sin_t, q_gain, B, L, H, q, k, v, stream);
-  }
+  // 8 head rows per work item, 3 CTAs of 256 threads per SM (80 registers): the fastest of the
+  // {4, 6, 8} rows x {2..6} CTAs/SM configurations measured at the 1024^2 shape.
+  return launch_rows<8, 3>(qkv, q_scale, k_scale, cos_t, sin_t, q_gain, B, L, H, q, k, v, stream);
 }
 
 }  // namespace flk
