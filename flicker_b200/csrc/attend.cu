@@ -90,12 +90,11 @@ __device__ __forceinline__ uint64_t desc_mnmajor(const uint8_t* tile, int kc) {
   return umma_desc_sw128(smem_u32(tile) + kc * 2048, kHalfBytes, 1024);
 }
 
-// exp of one 32-column chunk of a row of S -> 16 packed bf16x2 words of P, and the row sum of
-// the bf16-ROUNDED values (kernels.py:124-125 sums fp32(bf16(exp(s)))). One pair in
+// exp of one 32-column chunk of a row of S -> 16 packed bf16x2 words of P. One pair in
 // kPolyEvery goes through the FMA-pipe polynomial, the rest through MUFU.EX2, so the SFU is
 // not the only unit producing exponentials.
 constexpr int kPolyEvery = 4;
-__device__ __forceinline__ void exp_chunk(const uint32_t (&r)[32], uint32_t (&pk)[16], float2& l0, float2& l1) {
+__device__ __forceinline__ void exp_chunk(const uint32_t (&r)[32], uint32_t (&pk)[16]) {
   const float2 log2e = make_float2(kLog2e, kLog2e);
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
@@ -108,6 +107,14 @@ __device__ __forceinline__ void exp_chunk(const uint32_t (&r)[32], uint32_t (&pk
       e.y = ex2_approx(x.y);
     }
     pk[i] = pack_bf16x2(e.x, e.y);
+  }
+}
+
+// Row sum of the bf16-ROUNDED P values of one chunk (kernels.py:124-125 sums fp32(bf16(exp(s)))),
+// done after P is in TMEM and handed to the issuer, i.e. off the softmax -> P.V critical path.
+__device__ __forceinline__ void row_sum_chunk(const uint32_t (&pk)[16], float2& l0, float2& l1) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
     const float2 rounded = make_float2(__uint_as_float(pk[i] << 16), __uint_as_float(pk[i] & 0xFFFF0000u));
     if (i & 1)
       l1 = __fadd2_rn(l1, rounded);
@@ -279,21 +286,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         // Two 32-column chunks of this row's half of S; chunk 1 is loading while chunk 0 is
         // exponentiated, and each chunk's P is handed to the issuer as soon as it is in TMEM.
-        uint32_t ra[32], rb[32], pk[16];
+        uint32_t ra[32], rb[32], pk0[16], pk1[16];
         tmem_ld_32x32b_x32(s_addr, ra);
         tmem_wait_ld(ra);
         tmem_ld_32x32b_x32(s_addr + 32, rb);
-        exp_chunk(ra, pk, l0, l1);
-        tmem_st_32x32b_x16(s_addr, pk);
+        exp_chunk(ra, pk0);
+        tmem_st_32x32b_x16(s_addr, pk0);
         tmem_wait_ld(rb);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&sm.p_part[t][0]);
-        exp_chunk(rb, pk, l0, l1);
-        tmem_st_32x32b_x16(s_addr + 16, pk);
+        exp_chunk(rb, pk1);
+        tmem_st_32x32b_x16(s_addr + 16, pk1);
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&sm.p_part[t][1]);
+        row_sum_chunk(pk0, l0, l1);
+        row_sum_chunk(pk1, l0, l1);
       }
       // Row sum over all 128 KV columns: this warp's half plus the other half's partial.
       sm.l_part[t][half][row] = (l0.x + l0.y) + (l1.x + l1.y);
