@@ -32,6 +32,11 @@ SIGNATURES = {
                           ctypes.c_size_t, ctypes.c_void_p]),
     "flk_attend_workspace_size": (ctypes.c_size_t, [_int, _int, _int, _int]),
     "flk_attend_noalloc": (_int, [_u16p, _u16p, _u16p, _int, _int, _int, _int, _u16p, ctypes.c_void_p]),
+    "flk_w8a8_quantize_act": (_int, [_u16p, _f32p, _int, _int, ctypes.c_void_p, _f32p, ctypes.c_void_p]),
+    "flk_w8a8_gemm": (_int, [ctypes.c_void_p, ctypes.c_void_p, _f32p, _f32p, _int, _int, _int, _u16p,
+                             ctypes.c_void_p]),
+    "flk_i8_gemm_s32": (_int, [ctypes.c_void_p, ctypes.c_void_p, _int, _int, _int, ctypes.c_void_p,
+                               ctypes.c_void_p]),
     "flk_logit_bound": (_int, [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_float), _int,
                                ctypes.POINTER(ctypes.c_float)]),
     "flk_device_status": (_int, []),

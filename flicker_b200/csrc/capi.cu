@@ -20,6 +20,10 @@ int launch_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B
                   int splits, void* workspace, int* status, cudaStream_t stream);
 int attend_splits(int B, int H, int S, int sms);
 size_t attend_workspace_bytes(int B, int H, int S, int splits);
+int launch_w8a8_gemm(const int8_t* xq, const int8_t* wq, const float* x_scale, const float* w_scale, int M, int N,
+                     int K, uint16_t* y, int32_t* acc_out, int* status, int sms, cudaStream_t stream);
+int launch_quantize_act(const uint16_t* x, const float* inv_s, int M, int K, int8_t* xq, float* x_scale,
+                        cudaStream_t stream);
 }  // namespace flk
 
 // Device status word: 0, or FLK_ERR_DEVICE_TIMEOUT after a bounded in-kernel wait ran out.
@@ -173,6 +177,49 @@ int flk_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, i
     }
   }
   return flk::launch_attend(q, k, v, B, H, S, o, splits, workspace, st->status, static_cast<cudaStream_t>(stream));
+}
+
+int flk_w8a8_quantize_act(const uint16_t* x, const float* inv_smooth, int M, int K, int8_t* xq, float* x_scale,
+                          void* stream) {
+  if (M < 0 || K < 0 || K % 8 != 0) return FLK_ERR_INVALID_ARGUMENT;
+  if (static_cast<long long>(M) * K == 0) return FLK_OK;
+  if (static_cast<long long>(M) * 32 > 0x7FFFFFFFLL) return FLK_ERR_UNSUPPORTED;
+  const void* ptrs[] = {x, inv_smooth, xq, x_scale};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return FLK_ERR_INVALID_ARGUMENT;
+  int err = FLK_OK;
+  if (!device_state(&err)) return err;
+  return flk::launch_quantize_act(x, inv_smooth, M, K, xq, x_scale, static_cast<cudaStream_t>(stream));
+}
+
+static int w8a8_checks(const void* a, const void* b, int M, int N, int K, const void* out) {
+  if (M < 0 || N < 0 || K <= 0 || K % 16 != 0) return FLK_ERR_INVALID_ARGUMENT;
+  const void* ptrs[] = {a, b, out};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return FLK_ERR_INVALID_ARGUMENT;
+  return FLK_OK;
+}
+
+int flk_w8a8_gemm(const int8_t* xq, const int8_t* wq, const float* x_scale, const float* w_scale, int M, int N, int K,
+                  uint16_t* y, void* stream) {
+  int err = w8a8_checks(xq, wq, M, N, K, y);
+  if (err != FLK_OK) return err;
+  if (x_scale == nullptr || w_scale == nullptr) return FLK_ERR_INVALID_ARGUMENT;
+  if (static_cast<long long>(M) * N == 0) return FLK_OK;
+  const DeviceState* st = device_state(&err);
+  if (!st) return err;
+  return flk::launch_w8a8_gemm(xq, wq, x_scale, w_scale, M, N, K, y, nullptr, st->status, st->sms,
+                               static_cast<cudaStream_t>(stream));
+}
+
+int flk_i8_gemm_s32(const int8_t* a, const int8_t* b, int M, int N, int K, int32_t* c, void* stream) {
+  int err = w8a8_checks(a, b, M, N, K, c);
+  if (err != FLK_OK) return err;
+  if (static_cast<long long>(M) * N == 0) return FLK_OK;
+  const DeviceState* st = device_state(&err);
+  if (!st) return err;
+  return flk::launch_w8a8_gemm(a, b, nullptr, nullptr, M, N, K, nullptr, c, st->status, st->sms,
+                               static_cast<cudaStream_t>(stream));
 }
 
 int flk_logit_bound(const float* q_scale, const float* k_scale, int D, float* bound) {

@@ -89,6 +89,28 @@ int flk_attend_noalloc(const uint16_t* q, const uint16_t* k, const uint16_t* v,
  */
 int flk_logit_bound(const float* q_scale, const float* k_scale, int D, float* bound);
 
+/*
+ * W8A8 SmoothQuant linear, step 1 (per token). No counterpart in the reference (flicker's linear
+ * is a bf16 x @ w, src/flicker/nn.py:13-14); arithmetic per SmoothQuant (Xiao et al., 2022):
+ *   x'[i,k] = float(x[i,k]) * inv_smooth[k];  x_scale[i] = max_k |x'[i,k]| / 127 (1 if 0);
+ *   xq[i,k] = clamp(rint(x'[i,k] / x_scale[i]), -127, 127)   (round half to even)
+ * x [M, K] bf16, inv_smooth [K] fp32, xq [M, K] int8, x_scale [M] fp32. K % 8 == 0.
+ */
+int flk_w8a8_quantize_act(const uint16_t* x, const float* inv_smooth, int M, int K,
+                          int8_t* xq, float* x_scale, void* stream);
+
+/*
+ * W8A8 SmoothQuant linear, step 2: y = bf16(float(xq @ wq^T) * (x_scale[i] * w_scale[n])) with
+ * int32 accumulation on the int8 tensor cores. xq [M, K] int8, wq [N, K] int8 (per-output-channel
+ * codes, K contiguous), x_scale [M], w_scale [N] fp32, y [M, N] bf16. K % 16 == 0.
+ * No counterpart in the reference.
+ */
+int flk_w8a8_gemm(const int8_t* xq, const int8_t* wq, const float* x_scale, const float* w_scale,
+                  int M, int N, int K, uint16_t* y, void* stream);
+
+/* The raw int32 accumulators c [M, N] = a [M, K] @ b [N, K]^T of the same kernel (verification). */
+int flk_i8_gemm_s32(const int8_t* a, const int8_t* b, int M, int N, int K, int32_t* c, void* stream);
+
 /* Reads (and clears) the device-side status word of the current device: 0 or FLK_ERR_DEVICE_TIMEOUT.
  * Synchronises the device. */
 int flk_device_status(void);

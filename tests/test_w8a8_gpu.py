@@ -1,0 +1,93 @@
+"""W8A8 SmoothQuant linear on the B200 against the oracle (oracle/smoothquant.py), through the C ABI.
+
+Bars: int8 codes and fp32 scales bit-exact; int32 accumulators bit-exact (checked against a
+float64 matmul, which is exact here: |acc| <= K * 127^2 < 2^53); bf16 outputs bit-exact to the
+oracle's dequantisation of those accumulators. Parity against flicker itself is unpinned (it has
+no int8 path); the error against the bf16 x @ w is reported as information.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import to_device, to_host
+from oracle import smoothquant as SQ
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+from flicker_b200 import w8a8  # noqa: E402
+
+
+def exact_acc(xq, wq, rows=None):
+    a = xq.astype(np.float64) if rows is None else xq[rows].astype(np.float64)
+    return (a @ wq.astype(np.float64).T).astype(np.int64)
+
+
+def dev_i8(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("m,k,n", [(256, 384, 512), (200, 208, 300), (128, 128, 256), (1, 16, 1),
+                                   (4608, 3072, 9216)])
+def test_pipeline_bit_exact(m, k, n):
+    x, w = SQ.make_inputs(m, k, n, seed=m + k + n)
+    s, inv_s, xq, sx, wq, sw = SQ.prepare(x, w)
+    if k % 8 == 0:
+        gq, gsx = w8a8.quantize_act(to_device(x), to_device(inv_s))
+        np.testing.assert_array_equal(gq.cpu().numpy(), xq)
+        np.testing.assert_array_equal(gsx.cpu().numpy().view(np.uint32), sx.view(np.uint32))
+    gwq, gsw = w8a8.quantize_weight(to_device(w), to_device(s))
+    np.testing.assert_array_equal(gwq.cpu().numpy(), wq)
+    np.testing.assert_array_equal(gsw.cpu().numpy().view(np.uint32), sw.view(np.uint32))
+    a, b = dev_i8(xq), dev_i8(wq)
+    acc = w8a8.gemm_s32(a, b)
+    y = w8a8.gemm(a, b, to_device(sx), to_device(sw))
+    torch.cuda.synchronize()
+    rows = np.arange(m) if m * n * k <= 2 ** 28 else np.sort(np.random.default_rng(0).choice(m, 96, replace=False))
+    want = exact_acc(xq, wq, rows)
+    got = acc.cpu().numpy()[rows]
+    np.testing.assert_array_equal(got, want)
+    yw = SQ.dequant(want, sx[rows], sw)
+    np.testing.assert_array_equal(to_host(y)[rows].view(np.uint16), yw.view(np.uint16))
+
+
+def test_full_accumulator_tile_columns_and_tail():
+    """Every output element of a multi-tile ragged shape checked (tails in M, N and K)."""
+    m, k, n = 300, 400, 600
+    rng = np.random.default_rng(1)
+    a = rng.integers(-127, 128, (m, k), dtype=np.int8)
+    b = rng.integers(-127, 128, (n, k), dtype=np.int8)
+    got = w8a8.gemm_s32(dev_i8(a), dev_i8(b)).cpu().numpy()
+    np.testing.assert_array_equal(got, exact_acc(a, b))
+
+
+def test_extreme_codes_do_not_overflow():
+    """All codes at +-127 with K = 3072: |acc| = 49.5e6, far inside int32."""
+    m, k, n = 128, 3072, 256
+    a = np.full((m, k), 127, np.int8)
+    b = np.full((n, k), -127, np.int8)
+    got = w8a8.gemm_s32(dev_i8(a), dev_i8(b)).cpu().numpy()
+    assert (got == -127 * 127 * k).all()
+
+
+def test_layer_against_bf16_linear_is_close():
+    """Information: the quantised layer against the bf16 x @ w of the same operands (config 4)."""
+    x, w = SQ.make_inputs(seed=4)
+    xd, wd = to_device(x), to_device(w)
+    layer = w8a8.SmoothQuantLinear.from_float(wd, xd.float().abs().amax(dim=0))
+    y = layer(xd).float()
+    ref = xd.float() @ wd.float()
+    rel = ((y - ref).norm() / ref.norm()).item()
+    print(f"W8A8 vs bf16 linear: relative Frobenius error {rel:.4f}")
+    assert rel < 0.05
+    from flicker_b200 import _lib
+    assert _lib.lib().flk_device_status() == 0
+
+
+def test_errors():
+    a = torch.zeros(16, 24, dtype=torch.int8, device="cuda")
+    with pytest.raises(ValueError, match="multiple of 16"):
+        w8a8.gemm(a, a, torch.ones(16, device="cuda"), torch.ones(16, device="cuda"))
+    with pytest.raises(ValueError, match="CUDA"):
+        w8a8.quantize_act(torch.zeros(4, 8, dtype=torch.bfloat16), torch.ones(8))
