@@ -273,6 +273,63 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const uint16_t* __res
   }
 }
 
+// Same arithmetic with the row held in registers: every load of the row is issued before any
+// math (kIters x 16 B per lane in flight), and the codes are computed from the registers.
+template <int kIters>
+__global__ void __launch_bounds__(256) quantize_act_reg_kernel(const uint16_t* __restrict__ x,
+                                                               const float* __restrict__ inv_s, int M, int K,
+                                                               int8_t* __restrict__ xq,
+                                                               float* __restrict__ x_scale) {
+  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;  // whole warp leaves together
+  const uint16_t* xr = x + static_cast<size_t>(row) * K;
+  uint4 v[kIters];
+#pragma unroll
+  for (int it = 0; it < kIters; ++it) {
+    const int c = lane * 8 + it * 256;
+    v[it] = c < K ? *reinterpret_cast<const uint4*>(xr + c) : make_uint4(0, 0, 0, 0);
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int it = 0; it < kIters; ++it) {
+    const int c = lane * 8 + it * 256;
+    if (c >= K) break;
+    const float4 s0 = __ldg(reinterpret_cast<const float4*>(inv_s + c));
+    const float4 s1 = __ldg(reinterpret_cast<const float4*>(inv_s + c + 4));
+    const uint32_t w[4] = {v[it].x, v[it].y, v[it].z, v[it].w};
+    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      amax = fmaxf(amax, fabsf(__fmul_rn(__uint_as_float(w[j] << 16), sv[2 * j])));
+      amax = fmaxf(amax, fabsf(__fmul_rn(__uint_as_float(w[j] & 0xFFFF0000u), sv[2 * j + 1])));
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  float scale = __fdiv_rn(amax, 127.0f);
+  if (!(scale > 0.f)) scale = 1.0f;
+  if (lane == 0) x_scale[row] = scale;
+  int8_t* qr = xq + static_cast<size_t>(row) * K;
+#pragma unroll
+  for (int it = 0; it < kIters; ++it) {
+    const int c = lane * 8 + it * 256;
+    if (c >= K) break;
+    const float4 s0 = __ldg(reinterpret_cast<const float4*>(inv_s + c));
+    const float4 s1 = __ldg(reinterpret_cast<const float4*>(inv_s + c + 4));
+    const uint32_t w[4] = {v[it].x, v[it].y, v[it].z, v[it].w};
+    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float xv = (j & 1) ? __uint_as_float(w[j >> 1] & 0xFFFF0000u) : __uint_as_float(w[j >> 1] << 16);
+      const int qv = max(-127, min(127, __float2int_rn(__fdiv_rn(__fmul_rn(xv, sv[j]), scale))));
+      packed[j >> 2] |= (static_cast<uint32_t>(qv) & 0xFFu) << (8 * (j & 3));
+    }
+    *reinterpret_cast<uint2*>(qr + c) = make_uint2(packed[0], packed[1]);
+  }
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -340,8 +397,16 @@ int launch_w8a8_gemm(const int8_t* xq, const int8_t* wq, const float* x_scale, c
 int launch_quantize_act(const uint16_t* x, const float* inv_s, int M, int K, int8_t* xq, float* x_scale,
                         cudaStream_t stream) {
   const long long threads = static_cast<long long>(M) * 32;
-  quantize_act_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(x, inv_s, M, K, xq,
-                                                                                        x_scale);
+  const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+  // Rows up to 4096 wide are held in registers; wider rows take the two-pass kernel.
+  if (K <= 1024)
+    quantize_act_reg_kernel<4><<<blocks, 256, 0, stream>>>(x, inv_s, M, K, xq, x_scale);
+  else if (K <= 2048)
+    quantize_act_reg_kernel<8><<<blocks, 256, 0, stream>>>(x, inv_s, M, K, xq, x_scale);
+  else if (K <= 4096)
+    quantize_act_reg_kernel<16><<<blocks, 256, 0, stream>>>(x, inv_s, M, K, xq, x_scale);
+  else
+    quantize_act_kernel<<<blocks, 256, 0, stream>>>(x, inv_s, M, K, xq, x_scale);
   return cudaGetLastError() == cudaSuccess ? FLK_OK : FLK_ERR_CUDA;
 }
 

@@ -91,3 +91,15 @@ def test_errors():
         w8a8.gemm(a, a, torch.ones(16, device="cuda"), torch.ones(16, device="cuda"))
     with pytest.raises(ValueError, match="CUDA"):
         w8a8.quantize_act(torch.zeros(4, 8, dtype=torch.bfloat16), torch.ones(8))
+
+
+@pytest.mark.parametrize("m,k", [(64, 8), (33, 1000), (17, 2056), (9, 4096), (5, 4104)])
+def test_quantize_act_widths(m, k):
+    """Every row-width branch of the activation quantiser (register-held rows and the two-pass kernel)."""
+    rng = np.random.default_rng(k)
+    x = SQ.BF16 and rng.standard_normal((m, k)).astype(np.float32).astype(SQ.BF16)
+    inv_s = rng.uniform(0.2, 3.0, k).astype(np.float32)
+    want_q, want_s = SQ.quantize_act(x, inv_s)
+    gq, gs = w8a8.quantize_act(to_device(x), to_device(inv_s))
+    np.testing.assert_array_equal(gq.cpu().numpy(), want_q)
+    np.testing.assert_array_equal(gs.cpu().numpy().view(np.uint32), want_s.view(np.uint32))
