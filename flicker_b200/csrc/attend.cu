@@ -151,8 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < kSlots; ++s) mbar_init(&sm.kv_full[s], 1);
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sm.s_full[t], 1);
-      mbar_init(&sm.p_part[t][0], 32 * kSoftmaxWarps);
-      mbar_init(&sm.p_part[t][1], 32 * kSoftmaxWarps);
+      mbar_init(&sm.p_part[t][0], kSoftmaxWarps);  // one arrival per softmax warp
+      mbar_init(&sm.p_part[t][1], kSoftmaxWarps);
       mbar_init(&sm.o_full[t], 1);
     }
     mbar_init(&sm.drain, 1);
@@ -219,14 +219,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto qk = [&](int t, const uint8_t* kt) {
 #pragma unroll
       for (int kc = 0; kc < 8; ++kc)
-        umma_ss_if(leader, tmem + t * 128, desc_kmajor(sm.q[t], kc), desc_kmajor(kt, kc), kIdescQK, kc > 0);
+        umma_ss_warp(tmem + t * 128, desc_kmajor(sm.q[t], kc), desc_kmajor(kt, kc), kIdescQK, kc > 0);
     };
     bool ok = wait(&sm.q_full, 0) && kv_ready(0);
     if (ok) {
       tc_fence_after();
       for (int t = 0; t < nt; ++t) {
         qk(t, sm.kv[0]);  // S_t(0) = Q_t K_0^T
-        tc_commit_if(leader, &sm.s_full[t]);
+        tc_commit_warp(&sm.s_full[t]);
       }
     }
     for (int j = 0; ok && j < n_kv; ++j) {
@@ -246,13 +246,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int kc = (i & 1) + 2 * c + 4 * (i >> 1);  // kv rows [16kc, 16kc+16)
-            umma_ts_if(leader, tmem + 256 + t * 128, tmem + t * 128 + p_col(kc), desc_mnmajor(vt, kc), kIdescPV,
+            umma_ts_warp(tmem + 256 + t * 128, tmem + t * 128 + p_col(kc), desc_mnmajor(vt, kc), kIdescPV,
                        (j > 0 || c > 0 || i > 0) ? 1u : 0u);
           }
         }
         if (!ok) break;
         if (last) {
-          tc_commit_if(leader, &sm.o_full[t]);
+          tc_commit_warp(&sm.o_full[t]);
           continue;
         }
         if (t == 0) {
@@ -260,12 +260,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) break;
         }
         qk(t, kt);  // S_t(j+1) = Q_t K_{j+1}^T, written over P_t(j) after the P.V above has read it
-        tc_commit_if(leader, &sm.s_full[t]);
+        tc_commit_warp(&sm.s_full[t]);
       }
       if (!ok) break;
     }
     // Drain: every UMMA issued above has completed before TMEM is released.
-    tc_commit_if(leader, &sm.drain);
+    tc_commit_warp(&sm.drain);
     wait(&sm.drain, 0);
   } else {
     // ------------------------------------------------------------ softmax + epilogue
@@ -295,12 +295,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld(rb);
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&sm.p_part[t][0]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_part[t][0]);
         exp_chunk(rb, pk1);
         tmem_st_32x32b_x16(s_addr + 16, pk1);
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&sm.p_part[t][1]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_part[t][1]);
         row_sum_chunk(pk0, l0, l1);
         row_sum_chunk(pk1, l0, l1);
       }

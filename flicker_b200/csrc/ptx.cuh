@@ -72,27 +72,54 @@ __device__ __forceinline__ bool mbar_test_sleep(uint64_t* bar, uint32_t parity) 
   return ok != 0;
 }
 
+// Slow path of mbar_wait, kept out of line so that none of its work (the %globaltimer read,
+// the status-word load) is scheduled ahead of the first, usually successful, try_wait.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort, int* status) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t spin = 1; spin < kWaitSpinCap; ++spin) {
+    if (mbar_test_sleep(bar, parity)) return true;
+    if (*abort) return false;
+    if (*reinterpret_cast<volatile int*>(status) != 0) {
+      *abort = 1;
+      return false;
+    }
+    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+  }
+  *abort = 1;
+  atomicExch(status, kErrDeviceTimeout);
+  return false;
+}
+
+// Up to kFastSpins back-to-back try_waits (no suspend hint) in one PTX loop: a phase that
+// completes within a few microseconds is seen within ~150 cycles, and an already completed one
+// costs one try_wait. Returns whether the phase completed.
+constexpr uint32_t kFastSpins = 4096;
+__device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .u32 n;\n\t"
+      "mov.u32 n, 0;\n\t"
+      "SPIN_%=:\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "@p bra DONE_%=;\n\t"
+      "add.u32 n, n, 1;\n\t"
+      "setp.lt.u32 p, n, %3;\n\t"
+      "@p bra SPIN_%=;\n\t"
+      "DONE_%=:\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(kFastSpins)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with the given parity has completed. Returns false (after
 // recording the timeout in *status and raising *abort) if it does not within the
 // limit, or if another thread of the CTA or another CTA has already given up.
 // `status` is the library's device status word (0 = ok).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* status) {
   if (mbar_test(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t spin = 1; spin < kWaitSpinCap; ++spin) {
-    if (mbar_test_sleep(bar, parity)) return true;
-    {
-      if (*abort) return false;
-      if (*reinterpret_cast<volatile int*>(status) != 0) {
-        *abort = 1;
-        return false;
-      }
-      if (globaltimer_ns() - t0 > kWaitLimitNs) break;
-    }
-  }
-  *abort = 1;
-  atomicExch(status, kErrDeviceTimeout);
-  return false;
+  return mbar_wait_slow(bar, parity, abort, status);
 }
 
 // Named barrier `id` (1..15) over `count` threads (a multiple of 32).
@@ -162,35 +189,37 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
       : "memory");
 }
 
-// Warp-converged forms: every lane of the warp executes the instruction stream and only the
-// lane with `leader` set issues (keeps the issuing warp converged, like elect.sync issue).
-__device__ __forceinline__ void umma_ss_if(bool leader, uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                           uint32_t idesc, uint32_t accumulate) {
+// Warp-collective forms: all 32 lanes of a converged warp execute the instruction and
+// elect.sync picks the one lane that issues it. Issued this way a tcgen05.mma costs the
+// issuing warp ~15-20 cycles and up to ~8 MMAs queue ahead of the tensor pipe; the same
+// MMA issued from a lane-predicated or single-thread region costs ~60 cycles, about its own
+// execution time (128x128x16), so the issuer could never run ahead of the pipe.
+__device__ __forceinline__ void umma_ss_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p, l;\n\t"
+      "{\n\t.reg .pred p, e;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "setp.ne.b32 l, %5, 0;\n\t"
-      "@l tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(static_cast<uint32_t>(leader))
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-__device__ __forceinline__ void umma_ts_if(bool leader, uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                           uint32_t idesc, uint32_t accumulate) {
+__device__ __forceinline__ void umma_ts_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p, l;\n\t"
+      "{\n\t.reg .pred p, e;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "setp.ne.b32 l, %5, 0;\n\t"
-      "@l tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(static_cast<uint32_t>(leader))
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-__device__ __forceinline__ void tc_commit_if(bool leader, uint64_t* bar) {
+__device__ __forceinline__ void tc_commit_warp(uint64_t* bar) {
   asm volatile(
-      "{\n\t.reg .pred l;\n\t"
-      "setp.ne.b32 l, %1, 0;\n\t"
-      "@l tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(
-          smem_u32(bar)),
-      "r"(static_cast<uint32_t>(leader))
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(
+          smem_u32(bar))
       : "memory");
 }
 
