@@ -287,9 +287,31 @@ def run_w8a8(args, rank, world):
                 "d2h_bytes_per_step": M * N * 2, "steps": e2e_steps, "ms_per_step": e2e_ms},
         "gpu_launches": 2 * steps, "clocks": clocks.summary, "device_status": _lib.lib().flk_device_status(),
     }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = w8a8_cpu_sample(sets[0], w, layer, rows=512)
     if rank == 0:
         print(json.dumps(line), flush=True)
     return 0
+
+
+def w8a8_cpu_sample(x, w, layer, rows: int):
+    """The oracle's per-step work (quantise activations, int GEMM, dequantise) on `rows` tokens, host cores."""
+    import numpy as np
+
+    from oracle import smoothquant as SQ
+
+    xs = x[:rows].float().cpu().numpy()
+    inv_s = layer.inv_s.cpu().numpy()
+    wq = layer.wq.cpu().numpy()
+    sw = layer.w_scale.cpu().numpy()
+    k, n = w.shape
+    t0 = time.perf_counter()
+    xq, sx = SQ.quantize_act(xs, inv_s)
+    y = SQ.dequant(SQ.int_gemm_blas(xq, wq), sx, sw)
+    dt = time.perf_counter() - t0
+    assert y.shape == (rows, n)
+    return {"value": 2.0 * rows * n * k / dt / 1e12, "unit": "TOPS", "cores": os.cpu_count() or 1, "kind": "port",
+            "sample": f"{rows} of 4608 tokens: numpy quantise + float64-BLAS exact int GEMM + dequantise"}
 
 
 # ------------------------------------------------------------------ our arm

@@ -90,29 +90,6 @@ static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parit
   return false;
 }
 
-// Up to kFastSpins back-to-back try_waits (no suspend hint) in one PTX loop: a phase that
-// completes within a few microseconds is seen within ~150 cycles, and an already completed one
-// costs one try_wait. Returns whether the phase completed.
-constexpr uint32_t kFastSpins = 4096;
-__device__ __forceinline__ bool mbar_spin(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .u32 n;\n\t"
-      "mov.u32 n, 0;\n\t"
-      "SPIN_%=:\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
-      "@p bra DONE_%=;\n\t"
-      "add.u32 n, n, 1;\n\t"
-      "setp.lt.u32 p, n, %3;\n\t"
-      "@p bra SPIN_%=;\n\t"
-      "DONE_%=:\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "n"(kFastSpins)
-      : "memory");
-  return ok != 0;
-}
-
 // Wait until the phase with the given parity has completed. Returns false (after
 // recording the timeout in *status and raising *abort) if it does not within the
 // limit, or if another thread of the CTA or another CTA has already given up.

@@ -92,6 +92,11 @@ def int_gemm(xq: np.ndarray, wq_nk: np.ndarray, rows: np.ndarray | None = None) 
     return a @ np.asarray(wq_nk, np.int64).T
 
 
+def int_gemm_blas(xq: np.ndarray, wq_nk: np.ndarray) -> np.ndarray:
+    """acc = Xq @ Wq^T through a float64 BLAS matmul, exact while |acc| < 2^53 (the CPU baseline's GEMM)."""
+    return (np.asarray(xq, np.float64) @ np.asarray(wq_nk, np.float64).T).astype(np.int64)
+
+
 def dequant(acc: np.ndarray, sx: np.ndarray, sw: np.ndarray) -> np.ndarray:
     """y = bf16(float32(acc) * float32(sx[i] * sw[n]))."""
     scale = (np.asarray(sx, F32)[:, None] * np.asarray(sw, F32)[None, :]).astype(F32)
