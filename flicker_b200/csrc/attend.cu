@@ -81,15 +81,6 @@ __device__ __forceinline__ Smem* smem_ptr(uint8_t* raw) {
   return reinterpret_cast<Smem*>(a);
 }
 
-// K-major operand (rows of 128 bf16 split in two 64-column swizzled boxes): K-chunk kc of 16.
-__device__ __forceinline__ uint64_t desc_kmajor(const uint8_t* tile, int kc) {
-  return umma_desc_sw128(smem_u32(tile) + (kc >> 2) * kHalfBytes + (kc & 3) * 32, 16, 1024);
-}
-// MN-major B operand (V): K-chunk kc = KV rows [16kc, 16kc+16); N = head dim over both boxes.
-__device__ __forceinline__ uint64_t desc_mnmajor(const uint8_t* tile, int kc) {
-  return umma_desc_sw128(smem_u32(tile) + kc * 2048, kHalfBytes, 1024);
-}
-
 // exp of one 32-column chunk of a row of S -> 16 packed bf16x2 words of P. One pair in
 // kPolyEvery goes through the FMA-pipe polynomial, the rest through MUFU.EX2, so the SFU is
 // not the only unit producing exponentials.
@@ -127,6 +118,42 @@ __device__ __forceinline__ void row_sum_chunk(const uint32_t (&pk)[16], float2& 
 // the softmax warp of column half h writes the P of S columns [64h, 64h+64) packed into
 // columns [64h, 64h+32), i.e. over S columns it has already read.
 __device__ __forceinline__ uint32_t p_col(int kc) { return static_cast<uint32_t>((kc >> 2) * 64 + (kc & 3) * 8); }
+
+// Epilogue of one softmax warp: its 32 rows x 64 columns of O from TMEM, either normalised and
+// rounded to bf16 (o = bf16(acc / l), kernels.py:130) or, for a KV split, the fp32 partials.
+// Kept out of line so that this once-per-CTA code sits apart from the KV loop's code.
+__device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t grow, int half, int split, float l) {
+  if (p.n_splits == 1) {
+    uint16_t* orow = p.o + grow * kDim + half * 64;
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(o_addr + c * 32, r);
+      tmem_wait_ld(r);
+      uint32_t pk[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        pk[i] = pack_bf16x2(__fdiv_rn(__uint_as_float(r[2 * i]), l), __fdiv_rn(__uint_as_float(r[2 * i + 1]), l));
+      uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+    }
+  } else {
+    // Partial result of this split: un-normalised fp32 accumulator and row sum.
+    const size_t plane = static_cast<size_t>(gridDim.y) * p.S;  // rows per split
+    float* arow = p.acc + (split * plane + grow) * kDim + half * 64;
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(o_addr + c * 32, r);
+      tmem_wait_ld(r);
+      uint4* dst = reinterpret_cast<uint4*>(arow + c * 32);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dst[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
+    }
+    if (half == 0) p.lsum[split * plane + grow] = l;
+  }
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
     attend_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
@@ -194,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (n >= kSlots) {
         const int m = n - kSlots;
         const int done = (m & 1) ? (m >> 1) + 1 : (m >> 1);  // completion index of slot_free to await
-        if (!__all_sync(0xffffffffu, mbar_wait(slot_free, done & 1, abort, p.status))) break;
+        if (!mbar_wait_warp(slot_free, done & 1, abort, p.status)) break;
       }
       if (leader) {
         mbar_arrive_expect_tx(&sm.kv_full[slot], kTileBytes);
@@ -211,43 +238,56 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < kSlots; ++s)
       if (issued[s] > 0) mbar_wait(&sm.kv_full[s], (issued[s] - 1) & 1, abort, p.status);
   } else if (warp == 1) {
-    // ------------------------------------------------------------ UMMA issuer (whole warp, lane 0 issues)
-    auto wait = [&](uint64_t* bar, uint32_t parity) {
-      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, p.status));
-    };
+    // ------------------------------------------------------------ UMMA issuer (whole warp, elect.sync issues)
+    auto wait = [&](uint64_t* bar, uint32_t parity) { return mbar_wait_warp(bar, parity, abort, p.status); };
     auto kv_ready = [&](int n) { return wait(&sm.kv_full[n % kSlots], (n / kSlots) & 1); };
-    auto qk = [&](int t, const uint8_t* kt) {
+    // Descriptor low words: Q tile t, K-major ring slot, MN-major (V) ring slot; chunk kc, slot and
+    // tile offsets are added to the start field (units of 16 bytes).
+    const uint32_t q_lo = umma_desc_lo(smem_u32(sm.q[0]), 16);
+    const uint32_t k_lo = umma_desc_lo(smem_u32(sm.kv[0]), 16);
+    const uint32_t v_lo = umma_desc_lo(smem_u32(sm.kv[0]), kHalfBytes);
+    constexpr uint32_t kTile16 = kTileBytes >> 4;
+    auto qk = [&](int t, int slot) {  // S_t = Q_t K^T from ring slot `slot`
 #pragma unroll
-      for (int kc = 0; kc < 8; ++kc)
-        umma_ss_warp(tmem + t * 128, desc_kmajor(sm.q[t], kc), desc_kmajor(kt, kc), kIdescQK, kc > 0);
+      for (int kc = 0; kc < 8; ++kc) {
+        const uint32_t kcoff = (kc >> 2) * (kHalfBytes >> 4) + (kc & 3) * 2;
+        umma_ss_warp_lo(tmem + t * 128, q_lo + t * kTile16 + kcoff, k_lo + slot * kTile16 + kcoff, kIdescQK,
+                        kc > 0);
+      }
     };
     bool ok = wait(&sm.q_full, 0) && kv_ready(0);
     if (ok) {
       tc_fence_after();
-      for (int t = 0; t < nt; ++t) {
-        qk(t, sm.kv[0]);  // S_t(0) = Q_t K_0^T
-        tc_commit_warp(&sm.s_full[t]);
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (t < nt) {
+          qk(t, 0);  // S_t(0) = Q_t K_0^T
+          tc_commit_warp(&sm.s_full[t]);
+        }
       }
     }
     for (int j = 0; ok && j < n_kv; ++j) {
       const int nv = 2 * j + 1, nk = 2 * j + 2;
       const bool last = (j == n_kv - 1);
-      ok = kv_ready(nv);
+      ok = kv_ready(nv) && (last || kv_ready(nk));
       if (!ok) break;
-      const uint8_t* vt = sm.kv[nv % kSlots];
-      const uint8_t* kt = sm.kv[nk % kSlots];
-      for (int t = 0; t < nt; ++t) {
+      const uint32_t vslot = v_lo + (nv % kSlots) * kTile16;
+      const int kslot = nk % kSlots;
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (t >= nt) break;
         // P.V in two steps: K-chunks {0,1,4,5} (P chunk 0 of both column halves) as soon as every
         // softmax warp has written its first chunk, then {2,3,6,7}.
-        for (int c = 0; c < 2 && ok; ++c) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
           ok = wait(&sm.p_part[t][c], j & 1);
           if (!ok) break;
           tc_fence_after();
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             const int kc = (i & 1) + 2 * c + 4 * (i >> 1);  // kv rows [16kc, 16kc+16)
-            umma_ts_warp(tmem + 256 + t * 128, tmem + t * 128 + p_col(kc), desc_mnmajor(vt, kc), kIdescPV,
-                       (j > 0 || c > 0 || i > 0) ? 1u : 0u);
+            umma_ts_warp_lo(tmem + 256 + t * 128, tmem + t * 128 + p_col(kc), vslot + kc * (2048 >> 4), kIdescPV,
+                            (j > 0 || c > 0 || i > 0) ? 1u : 0u);
           }
         }
         if (!ok) break;
@@ -255,11 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_commit_warp(&sm.o_full[t]);
           continue;
         }
-        if (t == 0) {
-          ok = kv_ready(nk);
-          if (!ok) break;
-        }
-        qk(t, kt);  // S_t(j+1) = Q_t K_{j+1}^T, written over P_t(j) after the P.V above has read it
+        qk(t, kslot);  // S_t(j+1) = Q_t K_{j+1}^T, written over P_t(j) after the P.V above has read it
         tc_commit_warp(&sm.s_full[t]);
       }
       if (!ok) break;
@@ -281,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int j = 0; j < n_kv; ++j) {
         // Warp-uniform outcome: the tcgen05.ld/st below are .sync.aligned.
-        ok = __all_sync(0xffffffffu, mbar_wait(&sm.s_full[t], j & 1, abort, p.status));
+        ok = mbar_wait_warp(&sm.s_full[t], j & 1, abort, p.status);
         if (!ok) break;
         tc_fence_after();
         // Two 32-column chunks of this row's half of S; chunk 1 is loading while chunk 0 is
@@ -310,42 +346,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       sm.l_part[t][half][row] = (l0.x + l0.y) + (l1.x + l1.y);
       named_barrier_sync(1 + t, 32 * kSoftmaxWarps);
       const float l = sm.l_part[t][0][row] + sm.l_part[t][1][row];
-      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&sm.o_full[t], 0, abort, p.status));
+      if (ok) ok = mbar_wait_warp(&sm.o_full[t], 0, abort, p.status);
       if (ok) {
         tc_fence_after();
         const uint32_t o_addr = tmem + lane_off + 256 + t * 128 + half * 64;
         const size_t grow = static_cast<size_t>(row_base) + (t0 + t) * kTile + row;  // global query row
-        if (p.n_splits == 1) {
-          uint16_t* orow = p.o + grow * kDim + half * 64;
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(o_addr + c * 32, r);
-            tmem_wait_ld(r);
-            uint32_t pk[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-              pk[i] = pack_bf16x2(__fdiv_rn(__uint_as_float(r[2 * i]), l),
-                                  __fdiv_rn(__uint_as_float(r[2 * i + 1]), l));
-            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
-          }
-        } else {
-          // Partial result of this split: un-normalised fp32 accumulator and row sum.
-          const size_t plane = static_cast<size_t>(gridDim.y) * p.S;  // rows per split
-          float* arow = p.acc + (split * plane + grow) * kDim + half * 64;
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(o_addr + c * 32, r);
-            tmem_wait_ld(r);
-            uint4* dst = reinterpret_cast<uint4*>(arow + c * 32);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) dst[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
-          }
-          if (half == 0) p.lsum[split * plane + grow] = l;
-        }
+        store_rows(p, o_addr, grow, half, split, l);
       }
     }
   }

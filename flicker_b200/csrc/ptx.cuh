@@ -73,17 +73,23 @@ __device__ __forceinline__ bool mbar_test_sleep(uint64_t* bar, uint32_t parity) 
 }
 
 // Slow path of mbar_wait, kept out of line so that none of its work (the %globaltimer read,
-// the status-word load) is scheduled ahead of the first, usually successful, try_wait.
+// the status-word load) is scheduled ahead of the first, usually successful, try_wait. Between
+// sleeping polls only the CTA's abort flag (shared memory) is read; the device status word (a
+// global load of several hundred cycles, during which a completed phase would go unnoticed) and
+// the clock are read every kPollsPerCheck polls.
+constexpr uint32_t kPollsPerCheck = 64;
 static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort, int* status) {
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t spin = 1; spin < kWaitSpinCap; ++spin) {
     if (mbar_test_sleep(bar, parity)) return true;
     if (*abort) return false;
-    if (*reinterpret_cast<volatile int*>(status) != 0) {
-      *abort = 1;
-      return false;
+    if (spin % kPollsPerCheck == 0) {
+      if (*reinterpret_cast<volatile int*>(status) != 0) {
+        *abort = 1;
+        return false;
+      }
+      if (globaltimer_ns() - t0 > kWaitLimitNs) break;
     }
-    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
   }
   *abort = 1;
   atomicExch(status, kErrDeviceTimeout);
@@ -97,6 +103,14 @@ static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parit
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* status) {
   if (mbar_test(bar, parity)) return true;
   return mbar_wait_slow(bar, parity, abort, status);
+}
+
+// mbar_wait for all 32 lanes of a converged warp, with a warp-uniform outcome: one vote on a
+// single try_wait decides the common case without divergent code; the lanes go to the slow
+// path together only when the phase is still open.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort, int* status) {
+  if (__all_sync(0xffffffffu, mbar_test(bar, parity))) return true;
+  return __all_sync(0xffffffffu, mbar_wait_slow(bar, parity, abort, status)) != 0;
 }
 
 // Named barrier `id` (1..15) over `count` threads (a multiple of 32).
@@ -197,6 +211,38 @@ __device__ __forceinline__ void tc_commit_warp(uint64_t* bar) {
       "elect.sync _|e, 0xffffffff;\n\t"
       "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(
           smem_u32(bar))
+      : "memory");
+}
+
+// The same MMAs with the shared-memory descriptors given as their low 32-bit words (start >> 4,
+// LBO >> 4 << 16) over the fixed high word kDescHiSw128 (SBO 1024 B, version 1, 128-byte
+// swizzle): a caller advances a descriptor to another K chunk, ring slot or tile by adding to
+// the start field with one 32-bit add instead of rebuilding 64-bit descriptors per MMA.
+constexpr uint32_t kDescHiSw128 = (1024u >> 4) | (1u << 14) | (2u << 29);
+__device__ __forceinline__ uint32_t umma_desc_lo(uint32_t saddr, uint32_t lbo_bytes) {
+  return ((saddr >> 4) & 0x3FFFu) | (((lbo_bytes >> 4) & 0x3FFFu) << 16);
+}
+__device__ __forceinline__ void umma_ss_warp_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b64 da, db;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "mov.b64 da, {%1, %5};\n\t"
+      "mov.b64 db, {%2, %5};\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "n"(kDescHiSw128)
+      : "memory");
+}
+__device__ __forceinline__ void umma_ts_warp_lo(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t.reg .b64 db;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "mov.b64 db, {%2, %5};\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(idesc), "r"(accumulate), "n"(kDescHiSw128)
       : "memory");
 }
 
