@@ -58,8 +58,9 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end leg (default K/10)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-heads", type=int, default=4, help="heads in the CPU-baseline sample")
-    ap.add_argument("--workload", choices=["attention", "w8a8"], default="attention",
-                    help="attention: qk_prep + attend (the headline); w8a8: the SmoothQuant linear of config 4")
+    ap.add_argument("--workload", choices=["attention", "w8a8", "double"], default="attention",
+                    help="attention: qk_prep + attend (the headline); w8a8: the SmoothQuant linear of config 4; "
+                         "double: a double block's attention section with the fused concat and merged heads")
     return ap.parse_args()
 
 
@@ -314,6 +315,154 @@ def w8a8_cpu_sample(x, w, layer, rows: int):
             "sample": f"{rows} of 4608 tokens: numpy quantise + float64-BLAS exact int GEMM + dequantise"}
 
 
+# ------------------------------------------------------------------ double-block attention section
+def run_double(args, rank, world):
+    """One step = a double block's attention section (modules.py:127-138,157): the text and image
+    streams' qk_prep written into the joint q, k, v, then attention with merged heads. The same
+    section as the reference composes it (two qk_prep, concatenate, attend, merge_heads) is timed
+    beside it on the same inputs. Runs on rank 0; other ranks exit."""
+    if rank != 0:
+        return 0
+    import torch
+
+    import flicker_b200 as fb
+
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    H = NUM_HEADS
+    sets = []
+    for i in range(2):
+        qkv, qs, ks, freqs = make_inputs(torch, args.config, 1, H, 100 * i, dev)
+        g = torch.Generator(device=dev)
+        g.manual_seed(100 * i + 7)
+        iqs = (torch.rand(HEAD_DIM, generator=g, device=dev) + 0.5).to(torch.bfloat16)
+        iks = (torch.rand(HEAD_DIM, generator=g, device=dev) + 0.5).to(torch.bfloat16)
+        # the joint qkv split into the text stream (first NUM_TXT tokens) and the image stream
+        sets.append((qkv[:, :NUM_TXT].contiguous(), qkv[:, NUM_TXT:].contiguous(), (qs, ks), (iqs, iks), freqs))
+    s = sets[0][0].shape[1] + sets[0][1].shape[1]
+    flops = attend_flops(1, s, H)
+    q, k, v = (torch.empty((1, H, s, HEAD_DIM), dtype=torch.bfloat16, device=dev) for _ in range(3))
+
+    def fused(i, rec=None):
+        txt, img, ts, isc, freqs = sets[i % 2]
+        ft = fb.Freqs(freqs.cos[:NUM_TXT], freqs.sin[:NUM_TXT], freqs.q_gain)
+        fi = fb.Freqs(freqs.cos[NUM_TXT:], freqs.sin[NUM_TXT:], freqs.q_gain)
+        if rec is not None:
+            rec[0].record()
+        fb.qk_prep_into(txt, *ts, ft, H, (q, k, v), 0)
+        fb.qk_prep_into(img, *isc, fi, H, (q, k, v), NUM_TXT)
+        if rec is not None:
+            rec[1].record()
+        o = fb.attend_merged(q, k, v)
+        if rec is not None:
+            rec[2].record()
+        return o
+
+    def unfused(i, rec=None):
+        txt, img, ts, isc, freqs = sets[i % 2]
+        ft = fb.Freqs(freqs.cos[:NUM_TXT], freqs.sin[:NUM_TXT], freqs.q_gain)
+        fi = fb.Freqs(freqs.cos[NUM_TXT:], freqs.sin[NUM_TXT:], freqs.q_gain)
+        if rec is not None:
+            rec[0].record()
+        a = fb.qk_prep(txt, *ts, ft, H)
+        c = fb.qk_prep(img, *isc, fi, H)
+        jq, jk, jv = (torch.cat([x, y], dim=2) for x, y in zip(a, c))
+        if rec is not None:
+            rec[1].record()
+        o = fb.attend(jq, jk, jv)
+        if rec is not None:
+            rec[2].record()
+        return o.transpose(1, 2).reshape(1, s, H * HEAD_DIM).contiguous()
+
+    o_f = fused(0)
+    o_u = unfused(0)
+    torch.cuda.synchronize()
+    if not torch.equal(o_f, o_u):
+        raise RuntimeError("fused and unfused double-block sections differ")
+    K = args.steps
+    result = {}
+    for name, fn in (("unfused", unfused), ("fused", fused)):
+        for i in range(max(3, args.warmup)):
+            fn(i)
+        recs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local_rank) as clocks:
+            torch.cuda.synchronize()
+            start.record()
+            for i in range(K):
+                fn(i, recs[i])
+            end.record()
+            torch.cuda.synchronize()
+        result[name] = {"ms": start.elapsed_time(end) / K,
+                        "prep_us": statistics.mean(r[0].elapsed_time(r[1]) for r in recs) * 1e3,
+                        "attend_us": statistics.mean(r[1].elapsed_time(r[2]) for r in recs) * 1e3,
+                        "clocks": clocks.summary}
+    status = fb.device_status()
+
+    # end to end through the public API: both streams' qkv, tables and scales from pinned host
+    # memory, the merged output back to pinned host memory
+    txt0, img0, ts0, is0, fr0 = sets[0]
+    hosts = [t.cpu().pin_memory() for t in (txt0, img0, fr0.cos, fr0.sin, *ts0, *is0)]
+    devs = [torch.empty_like(t, device=dev) for t in hosts]
+    h_out = torch.empty((1, s, H * HEAD_DIM), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        for d, h in zip(devs, hosts):
+            d.copy_(h, non_blocking=True)
+        dt, di, dc, dsn, a, b, c, e = devs
+        fb.qk_prep_into(dt, a, b, fb.Freqs(dc[:NUM_TXT], dsn[:NUM_TXT], fr0.q_gain), H, (q, k, v), 0)
+        fb.qk_prep_into(di, c, e, fb.Freqs(dc[NUM_TXT:], dsn[NUM_TXT:], fr0.q_gain), H, (q, k, v), NUM_TXT)
+        h_out.copy_(fb.attend_merged(q, k, v), non_blocking=True)
+
+    e2e_steps = args.e2e_steps or max(3, K // 10)
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    pk, pk_kind = peaks()
+    f = result["fused"]
+    at_tflops = flops / (f["attend_us"] * 1e-6) / 1e12
+    line = {
+        "metric": f"double-block attention section TFLOP/s @{args.config}² (txt {NUM_TXT} + img {s - NUM_TXT}, "
+                  f"H={H}): qk_prep into the joint buffers + attend with merged heads",
+        "value": flops / (f["ms"] * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": 1, "steps": K,
+        "warmup": max(3, args.warmup), "ms_per_step": f["ms"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "double-block attention section (two streams, joint attention, merged heads)",
+                   "batch": 1, "seq_len": s, "num_txt": NUM_TXT, "heads": H, "head_dim": HEAD_DIM,
+                   "l2": "2 alternating input sets; per-step footprint > 126 MB L2"},
+        "kernels": {"qk_prep_into x2": {"us": f["prep_us"],
+                                        "GB/s": qk_prep_bytes(1, s, H) / (f["prep_us"] * 1e-6) / 1e9},
+                    "attend_merged": {"us": f["attend_us"], "TFLOP/s": at_tflops}},
+        "unfused": {"ms_per_step": result["unfused"]["ms"], "prep_and_concat_us": result["unfused"]["prep_us"],
+                    "attend_us": result["unfused"]["attend_us"],
+                    "merge_heads_us": result["unfused"]["ms"] * 1e3 - result["unfused"]["prep_us"]
+                    - result["unfused"]["attend_us"],
+                    "speedup_fused": result["unfused"]["ms"] / f["ms"]},
+        "roofline": {"bound": "tensor", "achieved": at_tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": at_tflops / pk["bf16_tflops"], "traffic": None, "kernel": "attend (merged store)",
+                     "peak_source": f"{pk_kind} bf16 burst (cuBLAS)"},
+        "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in hosts),
+                "d2h_bytes_per_step": h_out.numel() * 2, "steps": e2e_steps, "ms_per_step": e2e_ms},
+        "gpu_launches": 3 * K, "clocks": f["clocks"], "device_status": status,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        times, fl, threads, _ = cpu_sample(args.config, args.cpu_heads, reps=1)
+        line["cpu_baseline"] = {
+            "value": fl / times[0] / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{args.cpu_heads} of {H} heads, batch 1, S={s}: plain-XLA path restated in torch fp32"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # ------------------------------------------------------------------ our arm
 def main():
     args = parse_args()
@@ -324,6 +473,8 @@ def main():
         return run_reference(args, rank, world)
     if args.workload == "w8a8":
         return run_w8a8(args, rank, world)
+    if args.workload == "double":
+        return run_double(args, rank, world)
 
     import datetime
 

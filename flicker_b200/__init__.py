@@ -6,8 +6,8 @@
 splits one call across GPUs. The kernels live in ``libflicker_b200.so`` (C ABI in
 ``include/flicker_b200.h``), built by ``python -m flicker_b200.build``.
 """
-from .kernels import (EPS, EXP_LIMIT, ROW_TILES, SCORE_TILES, Freqs, attend, device_status, lane_pair,
-                      logit_bound, qk_prep, row_tile)
+from .kernels import (EPS, EXP_LIMIT, ROW_TILES, SCORE_TILES, Freqs, attend, attend_merged, device_status,
+                      double_qk_prep, lane_pair, logit_bound, qk_prep, qk_prep_into, row_tile)
 
-__all__ = ["EPS", "EXP_LIMIT", "ROW_TILES", "SCORE_TILES", "Freqs", "attend", "device_status", "lane_pair",
-           "logit_bound", "qk_prep", "row_tile"]
+__all__ = ["EPS", "EXP_LIMIT", "ROW_TILES", "SCORE_TILES", "Freqs", "attend", "attend_merged", "device_status",
+           "double_qk_prep", "lane_pair", "logit_bound", "qk_prep", "qk_prep_into", "row_tile"]

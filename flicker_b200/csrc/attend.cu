@@ -70,7 +70,9 @@ struct Params {
   int S;          // sequence length (multiple of 128)
   int n_tiles;    // S / 128
   int n_splits;   // KV splits (gridDim.z); 1 = the CTA normalises and writes o itself
-  uint16_t* o;    // [B*H*S, 128] bf16
+  int H;          // heads (locates a row of o in the merged layout)
+  int merged;     // 0: o is [B, H, S, 128]; 1: o is [B, S, H*128] (heads merged, kernels.attend + merge_heads)
+  uint16_t* o;    // bf16 output in the layout above
   float* acc;     // split > 1: [n_splits, B*H*S, 128] fp32 un-normalised partial P.V
   float* lsum;    // split > 1: [n_splits, B*H*S] fp32 partial row sums
   int* status;    // device status word
@@ -119,12 +121,22 @@ __device__ __forceinline__ void row_sum_chunk(const uint32_t (&pk)[16], float2& 
 // columns [64h, 64h+32), i.e. over S columns it has already read.
 __device__ __forceinline__ uint32_t p_col(int kc) { return static_cast<uint32_t>((kc >> 2) * 64 + (kc & 3) * 8); }
 
+// Row of o that holds query row `grow` (= (b * H + h) * S + s): itself in the head-major
+// [B, H, S, 128] layout; (b * S + s) * H + h when heads are merged into [B, S, H * 128]
+// (modules.merge_heads, src/flicker/modules.py:63-65).
+__device__ __forceinline__ size_t out_row(size_t grow, int S, int H, int merged) {
+  if (!merged) return grow;
+  const size_t bh = grow / S, s = grow - bh * S;
+  const size_t b = bh / H, h = bh - b * H;
+  return (b * S + s) * H + h;
+}
+
 // Epilogue of one softmax warp: its 32 rows x 64 columns of O from TMEM, either normalised and
 // rounded to bf16 (o = bf16(acc / l), kernels.py:130) or, for a KV split, the fp32 partials.
 // Kept out of line so that this once-per-CTA code sits apart from the KV loop's code.
 __device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t grow, int half, int split, float l) {
   if (p.n_splits == 1) {
-    uint16_t* orow = p.o + grow * kDim + half * 64;
+    uint16_t* orow = p.o + out_row(grow, p.S, p.H, p.merged) * kDim + half * 64;
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {
       uint32_t r[32];
@@ -367,7 +379,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // o = bf16(sum_s acc_s / sum_s l_s) over the KV splits; one thread per 8 output columns.
 __global__ void __launch_bounds__(256) combine_splits_kernel(const float* __restrict__ acc,
                                                              const float* __restrict__ lsum, int n_splits,
-                                                             long long rows, uint16_t* __restrict__ o) {
+                                                             long long rows, int S, int H, int merged,
+                                                             uint16_t* __restrict__ o) {
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= rows * (kDim / 8)) return;
   const long long row = idx / (kDim / 8);
@@ -384,7 +397,7 @@ __global__ void __launch_bounds__(256) combine_splits_kernel(const float* __rest
   uint32_t pk[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) pk[i] = pack_bf16x2(__fdiv_rn(a[2 * i], l), __fdiv_rn(a[2 * i + 1], l));
-  *reinterpret_cast<uint4*>(o + row * kDim + col) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  *reinterpret_cast<uint4*>(o + out_row(row, S, H, merged) * kDim + col) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
 }
 
 }  // namespace
@@ -440,8 +453,8 @@ size_t attend_workspace_bytes(int B, int H, int S, int splits) {
   return splits * rows * (kDim + 1) * sizeof(float);
 }
 
-int launch_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, uint16_t* o,
-                  int splits, void* workspace, int* status, cudaStream_t stream) {
+int launch_attend_layout(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, uint16_t* o,
+                         int merged, int splits, void* workspace, int* status, cudaStream_t stream) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return FLK_ERR_CUDA;
   static bool configured[64] = {};
@@ -460,6 +473,8 @@ int launch_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B
   p.S = S;
   p.n_tiles = S / kTile;
   p.n_splits = splits;
+  p.H = H;
+  p.merged = merged;
   p.o = o;
   p.acc = splits > 1 ? static_cast<float*>(workspace) : nullptr;
   p.lsum = splits > 1 ? p.acc + static_cast<size_t>(splits) * rows * kDim : nullptr;
@@ -469,11 +484,17 @@ int launch_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B
   if (cudaGetLastError() != cudaSuccess) return FLK_ERR_CUDA;
   if (splits > 1) {
     const long long threads = rows * (kDim / 8);
-    combine_splits_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(p.acc, p.lsum, splits,
-                                                                                              rows, o);
+    combine_splits_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
+        p.acc, p.lsum, splits, rows, S, H, merged, o);
     if (cudaGetLastError() != cudaSuccess) return FLK_ERR_CUDA;
   }
   return FLK_OK;
+}
+
+// Head-major output ([B, H, S, 128]), the layout of kernels.attend.
+int launch_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, uint16_t* o,
+                  int splits, void* workspace, int* status, cudaStream_t stream) {
+  return launch_attend_layout(q, k, v, B, H, S, o, 0, splits, workspace, status, stream);
 }
 
 }  // namespace flk

@@ -14,10 +14,10 @@
 
 namespace flk {
 int launch_qk_prep(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t* k_scale, const float* cos_t,
-                   const float* sin_t, float q_gain, int B, int L, int H, uint16_t* q, uint16_t* k, uint16_t* v,
-                   cudaStream_t stream);
-int launch_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, uint16_t* o,
-                  int splits, void* workspace, int* status, cudaStream_t stream);
+                   const float* sin_t, float q_gain, int B, int L, int H, int S_out, int row0, uint16_t* q,
+                   uint16_t* k, uint16_t* v, cudaStream_t stream);
+int launch_attend_layout(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, uint16_t* o,
+                         int merged, int splits, void* workspace, int* status, cudaStream_t stream);
 int attend_splits(int B, int H, int S, int sms);
 size_t attend_workspace_bytes(int B, int H, int S, int splits);
 int launch_w8a8_gemm(const int8_t* xq, const int8_t* wq, const float* x_scale, const float* w_scale, int M, int N,
@@ -131,10 +131,11 @@ const char* flk_error_string(int code) {
   }
 }
 
-int flk_qk_prep(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t* k_scale, const float* cos,
-                const float* sin, float q_gain, int B, int L, int H, int D, uint16_t* q, uint16_t* k, uint16_t* v,
-                void* stream) {
+static int qk_prep_entry(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t* k_scale, const float* cos,
+                         const float* sin, float q_gain, int B, int L, int H, int D, uint16_t* q, uint16_t* k,
+                         uint16_t* v, int S_out, int row0, void* stream) {
   if (B < 0 || L < 0 || H <= 0) return FLK_ERR_INVALID_ARGUMENT;
+  if (row0 < 0 || S_out < 0 || static_cast<long long>(row0) + L > S_out) return FLK_ERR_INVALID_ARGUMENT;
   if (D != 128) return FLK_ERR_UNSUPPORTED;
   if (!std::isfinite(q_gain)) return FLK_ERR_INVALID_ARGUMENT;
   if (static_cast<long long>(B) * L == 0) return FLK_OK;
@@ -143,8 +144,20 @@ int flk_qk_prep(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t* k_
     if (p == nullptr || !aligned16(p)) return FLK_ERR_INVALID_ARGUMENT;
   int err = FLK_OK;
   if (!device_state(&err)) return err;
-  return flk::launch_qk_prep(qkv, q_scale, k_scale, cos, sin, q_gain, B, L, H, q, k, v,
+  return flk::launch_qk_prep(qkv, q_scale, k_scale, cos, sin, q_gain, B, L, H, S_out, row0, q, k, v,
                              static_cast<cudaStream_t>(stream));
+}
+
+int flk_qk_prep(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t* k_scale, const float* cos,
+                const float* sin, float q_gain, int B, int L, int H, int D, uint16_t* q, uint16_t* k, uint16_t* v,
+                void* stream) {
+  return qk_prep_entry(qkv, q_scale, k_scale, cos, sin, q_gain, B, L, H, D, q, k, v, L, 0, stream);
+}
+
+int flk_qk_prep_into(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t* k_scale, const float* cos,
+                     const float* sin, float q_gain, int B, int L, int H, int D, uint16_t* q, uint16_t* k,
+                     uint16_t* v, int S_out, int row0, void* stream) {
+  return qk_prep_entry(qkv, q_scale, k_scale, cos, sin, q_gain, B, L, H, D, q, k, v, S_out, row0, stream);
 }
 
 size_t flk_attend_workspace_size(int B, int H, int S, int D) {
@@ -155,8 +168,8 @@ size_t flk_attend_workspace_size(int B, int H, int S, int D) {
   return flk::attend_workspace_bytes(B, H, S, flk::attend_splits(B, H, S, st->sms));
 }
 
-int flk_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, int D, uint16_t* o,
-               void* workspace, size_t ws_bytes, void* stream) {
+static int attend_entry(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, int D,
+                        uint16_t* o, int merged, void* workspace, size_t ws_bytes, void* stream) {
   int err = FLK_OK;
   if (!attend_shape_ok(B, H, S, D, &err)) return err;
   if (static_cast<long long>(B) * S == 0) return FLK_OK;
@@ -176,7 +189,18 @@ int flk_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, i
       return FLK_ERR_WORKSPACE;
     }
   }
-  return flk::launch_attend(q, k, v, B, H, S, o, splits, workspace, st->status, static_cast<cudaStream_t>(stream));
+  return flk::launch_attend_layout(q, k, v, B, H, S, o, merged, splits, workspace, st->status,
+                                   static_cast<cudaStream_t>(stream));
+}
+
+int flk_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, int D, uint16_t* o,
+               void* workspace, size_t ws_bytes, void* stream) {
+  return attend_entry(q, k, v, B, H, S, D, o, 0, workspace, ws_bytes, stream);
+}
+
+int flk_attend_merged(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, int D,
+                      uint16_t* o, void* workspace, size_t ws_bytes, void* stream) {
+  return attend_entry(q, k, v, B, H, S, D, o, 1, workspace, ws_bytes, stream);
 }
 
 int flk_w8a8_quantize_act(const uint16_t* x, const float* inv_smooth, int M, int K, int8_t* xq, float* x_scale,

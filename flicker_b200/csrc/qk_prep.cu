@@ -78,7 +78,8 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
     qk_prep_kernel(const uint16_t* __restrict__ qkv, const uint16_t* __restrict__ q_scale,
                    const uint16_t* __restrict__ k_scale, const float* __restrict__ cos_t,
                    const float* __restrict__ sin_t, float q_gain, int L, int H, int groups, long long n_items,
-                   uint16_t* __restrict__ q_out, uint16_t* __restrict__ k_out, uint16_t* __restrict__ v_out) {
+                   int S_out, int row0, uint16_t* __restrict__ q_out, uint16_t* __restrict__ k_out,
+                   uint16_t* __restrict__ v_out) {
   const long long item = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 4;
   const int lane16 = threadIdx.x & 15;
   const bool valid = item < n_items;
@@ -115,7 +116,9 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
     const int kind = r < H ? 0 : (r < 2 * H ? 1 : 2);  // uniform across the half-warp
     const int h = r - kind * H;
     if (!valid || r >= rows3) continue;
-    const size_t dst = ((static_cast<size_t>(b) * H + h) * L + l) * kHeadDim + col;
+    // Token l of this call is row row0 + l of the [B, H, S_out, D] outputs (row0 = 0, S_out = L
+    // for a plain call; a text or image stream writes its slice of the joint sequence).
+    const size_t dst = ((static_cast<size_t>(b) * H + h) * S_out + row0 + l) * kHeadDim + col;
     if (kind == 2) {  // v rows are copied straight through
       *reinterpret_cast<uint4*>(v_out + dst) = x[i];
       continue;
@@ -143,23 +146,23 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
 
 template <int kRows, int kMinBlocks>
 static int launch_rows(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t* k_scale, const float* cos_t,
-                       const float* sin_t, float q_gain, int B, int L, int H, uint16_t* q, uint16_t* k, uint16_t* v,
-                       cudaStream_t stream) {
+                       const float* sin_t, float q_gain, int B, int L, int H, int S_out, int row0, uint16_t* q,
+                       uint16_t* k, uint16_t* v, cudaStream_t stream) {
   const int groups = (3 * H + kRows - 1) / kRows;
   const long long n_items = static_cast<long long>(B) * L * groups;
   const long long blocks = (n_items * 16 + kThreads - 1) / kThreads;
   if (blocks > 0x7FFFFFFFLL) return FLK_ERR_UNSUPPORTED;
   qk_prep_kernel<kRows, kMinBlocks><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
-      qkv, q_scale, k_scale, cos_t, sin_t, q_gain, L, H, groups, n_items, q, k, v);
+      qkv, q_scale, k_scale, cos_t, sin_t, q_gain, L, H, groups, n_items, S_out, row0, q, k, v);
   return cudaGetLastError() == cudaSuccess ? FLK_OK : FLK_ERR_CUDA;
 }
 
 int launch_qk_prep(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t* k_scale, const float* cos_t,
-                   const float* sin_t, float q_gain, int B, int L, int H, uint16_t* q, uint16_t* k, uint16_t* v,
-                   cudaStream_t stream) {
+                   const float* sin_t, float q_gain, int B, int L, int H, int S_out, int row0, uint16_t* q,
+                   uint16_t* k, uint16_t* v, cudaStream_t stream) {
   // 8 head rows per work item, 3 CTAs of 256 threads per SM (80 registers): the fastest of the
   // {4, 6, 8} rows x {2..6} CTAs/SM configurations measured at the 1024^2 shape.
-  return launch_rows<8, 3>(qkv, q_scale, k_scale, cos_t, sin_t, q_gain, B, L, H, q, k, v, stream);
+  return launch_rows<8, 3>(qkv, q_scale, k_scale, cos_t, sin_t, q_gain, B, L, H, S_out, row0, q, k, v, stream);
 }
 
 }  // namespace flk

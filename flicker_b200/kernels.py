@@ -10,6 +10,14 @@ arrays, and the work runs in the sm_100a kernels of ``libflicker_b200.so``
 * ``Freqs``, ``EPS``, ``ROW_TILES``, ``row_tile``, ``lane_pair``, ``SCORE_TILES``,
   ``EXP_LIMIT``, ``logit_bound`` -- kernels.py:12-31,94-101
 
+Two fused forms of the callers' glue around them (no counterpart in kernels.py):
+
+* ``qk_prep_into`` / ``double_qk_prep`` -- the kernel branch of modules.double_prepare_qkv
+  (src/flicker/modules.py:127-138) with each stream's qk_prep writing straight into the joint
+  q, k, v instead of a jnp.concatenate copy afterwards;
+* ``attend_merged`` -- merge_heads(attend(q, k, v)) (modules.py:63-65,157,198) with the heads
+  merged by the attention epilogue's stores.
+
 There is no CPU or eager fallback: if the library is missing the call raises.
 """
 from __future__ import annotations
@@ -77,27 +85,8 @@ def _require_cuda_bf16(name: str, t: Array) -> None:
         raise ValueError(f"{name} must be bfloat16, got {t.dtype}")
 
 
-def qk_prep(
-    qkv: Array,
-    q_scale: Array,
-    k_scale: Array,
-    freqs: Freqs,
-    num_heads: int,
-    *,
-    rows: int | None = None,
-    interpret: bool = False,
-) -> tuple[Array, Array, Array]:
-    """Fused head transpose + QK-RMSNorm + RoPE (+ q gain) in one HBM pass.
-
-    ``qkv`` [B, L, 3*H*D] bf16 (columns ordered (3, H, D)) -> q, k, v [B, H, L, D] bf16.
-    ``q = bf16(q_gain * rope(fp32(bf16(rmsnorm(x)) * q_scale)))``, k likewise without the
-    gain, v copied (kernels.py:35-53). ``rows`` is the reference's row-tile hint: it is
-    validated exactly as kernels.py:71-73 does (``ValueError`` when no tile divides L);
-    the CUDA kernel does not need a row tile. ``interpret`` (Pallas interpret mode in the
-    reference) is not available.
-    """
-    if interpret:
-        raise NotImplementedError("interpret=True: this build runs only the sm_100a kernels")
+def _qk_prep_args(qkv: Array, q_scale: Array, k_scale: Array, freqs: Freqs, num_heads: int, rows: int | None):
+    """Validation shared by the qk_prep forms (kernels.py:66-73 error behaviour)."""
     _require_cuda_bf16("qkv", qkv)
     if qkv.dim() != 3:
         raise ValueError(f"qkv must be [B, L, 3*H*D], got shape {tuple(qkv.shape)}")
@@ -122,17 +111,124 @@ def qk_prep(
         if t.numel() != head_dim or t.device != qkv.device:
             raise ValueError(f"{name} must hold {head_dim} values on {qkv.device}")
         scales.append(t.reshape(head_dim).contiguous())
-    qkv = qkv.contiguous()
-    cos, sin = cos.contiguous(), sin.contiguous()
+    return qkv.contiguous(), scales, cos.contiguous(), sin.contiguous(), float(q_gain), batch, length, head_dim
+
+
+def qk_prep(
+    qkv: Array,
+    q_scale: Array,
+    k_scale: Array,
+    freqs: Freqs,
+    num_heads: int,
+    *,
+    rows: int | None = None,
+    interpret: bool = False,
+) -> tuple[Array, Array, Array]:
+    """Fused head transpose + QK-RMSNorm + RoPE (+ q gain) in one HBM pass.
+
+    ``qkv`` [B, L, 3*H*D] bf16 (columns ordered (3, H, D)) -> q, k, v [B, H, L, D] bf16.
+    ``q = bf16(q_gain * rope(fp32(bf16(rmsnorm(x)) * q_scale)))``, k likewise without the
+    gain, v copied (kernels.py:35-53). ``rows`` is the reference's row-tile hint: it is
+    validated exactly as kernels.py:71-73 does (``ValueError`` when no tile divides L);
+    the CUDA kernel does not need a row tile. ``interpret`` (Pallas interpret mode in the
+    reference) is not available.
+    """
+    if interpret:
+        raise NotImplementedError("interpret=True: this build runs only the sm_100a kernels")
+    qkv, scales, cos, sin, q_gain, batch, length, head_dim = _qk_prep_args(qkv, q_scale, k_scale, freqs,
+                                                                          num_heads, rows)
     out = [torch.empty((batch, num_heads, length, head_dim), dtype=qkv.dtype, device=qkv.device)
            for _ in range(3)]
     with torch.cuda.device(qkv.device):
         code = _lib.lib().flk_qk_prep(
             qkv.data_ptr(), scales[0].data_ptr(), scales[1].data_ptr(), cos.data_ptr(), sin.data_ptr(),
-            float(q_gain), batch, length, num_heads, head_dim,
+            q_gain, batch, length, num_heads, head_dim,
             out[0].data_ptr(), out[1].data_ptr(), out[2].data_ptr(), _stream(qkv))
     _lib.check("flk_qk_prep", code)
     return out[0], out[1], out[2]
+
+
+def qk_prep_into(qkv: Array, q_scale: Array, k_scale: Array, freqs: Freqs, num_heads: int,
+                 out: tuple[Array, Array, Array], row: int, *, rows: int | None = None) -> None:
+    """qk_prep writing token l of ``qkv`` to row ``row + l`` of ``out`` = (q, k, v) [B, H, S, D].
+
+    Same arithmetic, arguments and errors as ``qk_prep``; ``out`` must be contiguous bf16 of
+    the same batch/heads/head_dim with ``row + L <= S``. Rows outside [row, row + L) are left
+    untouched, so calls for the text and image streams fill one joint buffer.
+    """
+    qkv, scales, cos, sin, q_gain, batch, length, head_dim = _qk_prep_args(qkv, q_scale, k_scale, freqs,
+                                                                          num_heads, rows)
+    if len(out) != 3:
+        raise ValueError("out must be the (q, k, v) buffers")
+    seq = out[0].shape[2] if out[0].dim() == 4 else -1
+    for name, t in zip("qkv", out):
+        _require_cuda_bf16(f"out.{name}", t)
+        if (tuple(t.shape) != (batch, num_heads, seq, head_dim) or not t.is_contiguous()
+                or t.device != qkv.device):
+            raise ValueError(f"out.{name} must be a contiguous [B, H, S, D] = [{batch}, {num_heads}, S, "
+                             f"{head_dim}] tensor on {qkv.device}, got {tuple(t.shape)}")
+    if row < 0 or row + length > seq:
+        raise ValueError(f"rows [{row}, {row + length}) do not fit in S={seq}")
+    with torch.cuda.device(qkv.device):
+        code = _lib.lib().flk_qk_prep_into(
+            qkv.data_ptr(), scales[0].data_ptr(), scales[1].data_ptr(), cos.data_ptr(), sin.data_ptr(),
+            q_gain, batch, length, num_heads, head_dim,
+            out[0].data_ptr(), out[1].data_ptr(), out[2].data_ptr(), seq, row, _stream(qkv))
+    _lib.check("flk_qk_prep_into", code)
+
+
+def double_qk_prep(txt_qkv: Array, img_qkv: Array, txt_scales: tuple[Array, Array],
+                   img_scales: tuple[Array, Array], freqs: Freqs, num_heads: int) -> tuple[Array, Array, Array]:
+    """Joint q, k, v of a double block: text rows first, then image rows (modules.py:127-138).
+
+    ``freqs`` holds the lane tables of the joint sequence ([num_txt + num_img, 128]); the text
+    stream uses its first num_txt rows and the image stream the rest, as the reference slices
+    them. Equal to concatenating the two streams' ``qk_prep`` outputs along the sequence axis,
+    without that copy.
+    """
+    if txt_qkv.dim() != 3 or img_qkv.dim() != 3:
+        raise ValueError("txt_qkv and img_qkv must be [B, L, 3*H*D]")
+    num_txt, num_img = txt_qkv.shape[1], img_qkv.shape[1]
+    cos, sin, q_gain = freqs
+    if cos.shape[0] != num_txt + num_img or sin.shape[0] != num_txt + num_img:
+        raise ValueError(f"freqs must cover {num_txt} + {num_img} rows, got {tuple(cos.shape)}")
+    batch, width = txt_qkv.shape[0], txt_qkv.shape[2]
+    if img_qkv.shape[0] != batch or img_qkv.shape[2] != width or num_heads <= 0 or width % (3 * num_heads):
+        raise ValueError("txt_qkv and img_qkv must share batch and width 3 * num_heads * head_dim")
+    head_dim = width // (3 * num_heads)
+    out = tuple(torch.empty((batch, num_heads, num_txt + num_img, head_dim), dtype=txt_qkv.dtype,
+                            device=txt_qkv.device) for _ in range(3))
+    qk_prep_into(txt_qkv, *txt_scales, Freqs(cos[:num_txt], sin[:num_txt], q_gain), num_heads, out, 0)
+    qk_prep_into(img_qkv, *img_scales, Freqs(cos[num_txt:], sin[num_txt:], q_gain), num_heads, out, num_txt)
+    return out
+
+
+def _attend_args(q: Array, k: Array, v: Array, block: int | None):
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        _require_cuda_bf16(name, t)
+        if t.dim() != 4 or tuple(t.shape) != tuple(q.shape) or t.device != q.device:
+            raise ValueError(f"q, k, v must share one [B, H, S, D] shape and device; {name} is "
+                             f"{tuple(t.shape)}")
+    batch, heads, length, dim = q.shape
+    if dim != HEAD_DIM:
+        raise ValueError(f"head_dim must be {HEAD_DIM}, got {dim}")
+    if length % 128:
+        raise ValueError(f"attend needs S to be a multiple of 128, got {length}")
+    if block is not None and (block <= 0 or block % 128 or length % block):
+        raise ValueError(f"block={block} must be a multiple of 128 dividing S={length}")
+    return q.contiguous(), k.contiguous(), v.contiguous(), batch, heads, length, dim
+
+
+def _run_attend(fn: str, q: Array, k: Array, v: Array, o: Array, batch: int, heads: int, length: int,
+                dim: int) -> Array:
+    lib = _lib.lib()
+    with torch.cuda.device(q.device):
+        ws_bytes = lib.flk_attend_workspace_size(batch, heads, length, dim)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
+        code = getattr(lib, fn)(q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, length, dim,
+                                o.data_ptr(), ws.data_ptr() if ws is not None else None, ws_bytes, _stream(q))
+    _lib.check(fn, code)
+    return o
 
 
 def attend(q: Array, k: Array, v: Array, *, block: int | None = None, interpret: bool = False) -> Array:
@@ -146,29 +242,19 @@ def attend(q: Array, k: Array, v: Array, *, block: int | None = None, interpret:
     """
     if interpret:
         raise NotImplementedError("interpret=True: this build runs only the sm_100a kernels")
-    for name, t in (("q", q), ("k", k), ("v", v)):
-        _require_cuda_bf16(name, t)
-        if t.dim() != 4 or tuple(t.shape) != tuple(q.shape) or t.device != q.device:
-            raise ValueError(f"q, k, v must share one [B, H, S, D] shape and device; {name} is "
-                             f"{tuple(t.shape)}")
-    batch, heads, length, dim = q.shape
-    if dim != HEAD_DIM:
-        raise ValueError(f"head_dim must be {HEAD_DIM}, got {dim}")
-    if length % 128:
-        raise ValueError(f"attend needs S to be a multiple of 128, got {length}")
-    if block is not None and (block <= 0 or block % 128 or length % block):
-        raise ValueError(f"block={block} must be a multiple of 128 dividing S={length}")
-    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-    o = torch.empty_like(q)
-    lib = _lib.lib()
-    with torch.cuda.device(q.device):
-        ws_bytes = lib.flk_attend_workspace_size(batch, heads, length, dim)
-        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
-        code = lib.flk_attend(q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, length, dim,
-                              o.data_ptr(), ws.data_ptr() if ws is not None else None, ws_bytes,
-                              _stream(q))
-    _lib.check("flk_attend", code)
-    return o
+    q, k, v, batch, heads, length, dim = _attend_args(q, k, v, block)
+    return _run_attend("flk_attend", q, k, v, torch.empty_like(q), batch, heads, length, dim)
+
+
+def attend_merged(q: Array, k: Array, v: Array, *, block: int | None = None) -> Array:
+    """``merge_heads(attend(q, k, v))`` in one kernel: o [B, S, H*D] bf16 (modules.py:63-65).
+
+    Same arithmetic, arguments and errors as ``attend``; the epilogue stores each head's
+    columns into the merged rows, so there is no separate transpose pass over o.
+    """
+    q, k, v, batch, heads, length, dim = _attend_args(q, k, v, block)
+    o = torch.empty((batch, length, heads * dim), dtype=q.dtype, device=q.device)
+    return _run_attend("flk_attend_merged", q, k, v, o, batch, heads, length, dim)
 
 
 def device_status(device: torch.device | int | None = None) -> int:

@@ -54,6 +54,18 @@ int flk_qk_prep(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t* k_
                 uint16_t* q, uint16_t* k, uint16_t* v, void* stream);
 
 /*
+ * flk_qk_prep writing into a longer sequence: token l of this call goes to row row0 + l of
+ * q, k, v viewed as [B, H, S_out, D] (0 <= row0, row0 + L <= S_out). Two calls (text stream at
+ * row 0, image stream at row num_txt) build the joint q, k, v of a double block in place.
+ * Replaces the kernel branch of modules.double_prepare_qkv (src/flicker/modules.py:127-138):
+ * qkv_prep per stream, then jnp.concatenate([txt, img], axis=2), an extra HBM copy of q, k, v.
+ */
+int flk_qk_prep_into(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t* k_scale,
+                     const float* cos, const float* sin, float q_gain,
+                     int B, int L, int H, int D,
+                     uint16_t* q, uint16_t* k, uint16_t* v, int S_out, int row0, void* stream);
+
+/*
  * Bounded (max-free) non-causal attention, q pre-scaled by 1/sqrt(D).
  * Replaces flicker kernels.attend (src/flicker/kernels.py:105-145):
  *   p = bf16(exp(q k^T)),  l = sum_j fp32(p_j),  o = bf16((sum_j p_j v_j) / l)
@@ -64,6 +76,16 @@ int flk_qk_prep(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t* k_
 int flk_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                int B, int H, int S, int D, uint16_t* o,
                void* workspace, size_t ws_bytes, void* stream);
+
+/*
+ * flk_attend with the heads merged on output: o is [B, S, H*D] (head h in columns
+ * [h*D, (h+1)*D)), i.e. merge_heads(attend(q, k, v)) of modules.double_block / single_block
+ * (src/flicker/modules.py:157,198 with merge_heads :63-65) without the transpose pass.
+ * Same workspace rules as flk_attend.
+ */
+int flk_attend_merged(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                      int B, int H, int S, int D, uint16_t* o,
+                      void* workspace, size_t ws_bytes, void* stream);
 
 /* Bytes of workspace flk_attend needs for this shape on the current device. */
 size_t flk_attend_workspace_size(int B, int H, int S, int D);

@@ -99,3 +99,18 @@ def test_shape_checks_run_before_any_device_work():
     # non-finite gain
     assert lib.flk_qk_prep(fake, fake, fake, fake, fake, float("nan"), 1, 64, 2, 128, fake, fake, fake,
                            None) == _lib.FLK_ERR_INVALID_ARGUMENT
+    # qk_prep into a longer sequence: the rows must fit, row0 >= 0
+    assert lib.flk_qk_prep_into(fake, fake, fake, fake, fake, 1.0, 1, 64, 2, 128, fake, fake, fake, 100, 37,
+                                None) == _lib.FLK_ERR_INVALID_ARGUMENT
+    assert lib.flk_qk_prep_into(fake, fake, fake, fake, fake, 1.0, 1, 64, 2, 128, fake, fake, fake, 100, -1,
+                                None) == _lib.FLK_ERR_INVALID_ARGUMENT
+    assert lib.flk_qk_prep_into(fake, fake, fake, fake, fake, 1.0, 1, 64, 2, 64, fake, fake, fake, 100, 0,
+                                None) == _lib.FLK_ERR_UNSUPPORTED
+    assert lib.flk_qk_prep_into(fake, fake, fake, fake, fake, 1.0, 1, 0, 2, 128, fake, fake, fake, 100, 100,
+                                None) == 0
+    # merged-heads attend: the same shape rules as flk_attend
+    assert lib.flk_attend_merged(fake, fake, fake, 1, 2, 128, 64, fake, None, 0, None) == _lib.FLK_ERR_UNSUPPORTED
+    assert lib.flk_attend_merged(fake, fake, fake, 1, 2, 100, 128, fake, None, 0, None) \
+        == _lib.FLK_ERR_INVALID_ARGUMENT
+    assert lib.flk_attend_merged(odd, fake, fake, 1, 2, 128, 128, fake, None, 0, None) \
+        == _lib.FLK_ERR_INVALID_ARGUMENT
