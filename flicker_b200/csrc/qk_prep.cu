@@ -1,7 +1,7 @@
 // qk_prep for sm_100a: head split + QK-RMSNorm + lane-pair RoPE (+ q gain) in one HBM pass.
 //
 // Restates flicker kernels.qk_prep (src/flicker/kernels.py:57-91, body :35-53) as a
-// memory-bound CUDA kernel. Work item = one token x a group of 8 consecutive head rows
+// memory-bound CUDA kernel. Work item = one token x a group of 4 consecutive head rows
 // of that token's fused QKV row (row r of 3H: r < H -> q head r, r < 2H -> k head r-H,
 // else v head r-2H). A half-warp (16 lanes) owns one item; lane j owns columns
 // [8j, 8j+8) of every 128-wide head row, so:
@@ -10,10 +10,10 @@
 //     write side (the transpose costs nothing at row granularity);
 //   * the RoPE partner of column 2i is column 2i+1 of the same lane (no shuffle);
 //   * the cos/sin lane tables and both scale vectors are loaded once per item and reused
-//     for its 8 rows (they are L2-resident: 1 KB per token);
+//     for its rows (they are L2-resident: 1 KB per token);
 //   * the sum of squares is reduced across the 16 lanes with 4 xor-shuffles (q/k rows only;
 //     v rows are copied straight through);
-//   * all 8 row loads of an item are issued before any math (8 x 16 B in flight per lane).
+//   * all row loads of an item are issued before any math (4 x 16 B in flight per lane).
 // Rounding follows the reference body: fp32 norm (rsqrt on the SFU), bf16 round, bf16 x bf16
 // scale multiply rounded to bf16, fp32 rotation c*w + s*swap (no FMA contraction), q gain in
 // fp32, final bf16 round.
@@ -30,6 +30,26 @@ namespace {
 
 constexpr int kHeadDim = 128;
 constexpr int kThreads = 256;
+
+// Division of 32-bit unsigned values by a divisor fixed per launch (Granlund & Montgomery,
+// "Division by invariant integers using multiplication", 1994, figure 4.1): with
+// l = ceil(log2 d), m = floor(2^32 (2^l - d) / d) + 1, q = (t + ((n - t) >> 1)) >> (l - 1) where
+// t = mulhi(m, n), exact for every n < 2^32; d = 1 uses m = 0 and no shifts. The host builds it.
+struct FastDiv {
+  uint32_t m, s1, s2;
+  __device__ __forceinline__ uint32_t div(uint32_t n) const {
+    const uint32_t t = __umulhi(m, n);
+    return (t + ((n - t) >> s1)) >> s2;
+  }
+};
+
+FastDiv make_fast_div(uint32_t d) {
+  if (d <= 1) return FastDiv{0u, 0u, 0u};
+  uint32_t l = 0;
+  while ((1ull << l) < d) ++l;
+  const uint64_t m = ((1ull << 32) * ((1ull << l) - d)) / d + 1;
+  return FastDiv{static_cast<uint32_t>(m), 1u, l - 1};
+}
 
 __device__ __forceinline__ uint4 ld_stream(const uint16_t* p) {
   uint4 r;
@@ -77,17 +97,19 @@ template <int kRows, int kMinBlocks>
 __global__ void __launch_bounds__(kThreads, kMinBlocks)
     qk_prep_kernel(const uint16_t* __restrict__ qkv, const uint16_t* __restrict__ q_scale,
                    const uint16_t* __restrict__ k_scale, const float* __restrict__ cos_t,
-                   const float* __restrict__ sin_t, float q_gain, int L, int H, int groups, long long n_items,
-                   int S_out, int row0, uint16_t* __restrict__ q_out, uint16_t* __restrict__ k_out,
-                   uint16_t* __restrict__ v_out) {
-  const long long item = (static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x) >> 4;
+                   const float* __restrict__ sin_t, float q_gain, int L, int H, int groups, uint32_t n_items,
+                   FastDiv div_groups, FastDiv div_L, int S_out, int row0, uint16_t* __restrict__ q_out,
+                   uint16_t* __restrict__ k_out, uint16_t* __restrict__ v_out) {
+  // 32-bit index math throughout (the host keeps 16 * n_items below 2^31).
+  const uint32_t item = (blockIdx.x * kThreads + threadIdx.x) >> 4;
   const int lane16 = threadIdx.x & 15;
   const bool valid = item < n_items;
-  const long long it = valid ? item : 0;  // clamped so the index math below stays in range
-  const long long token = it / groups;    // b * L + l
+  const uint32_t it = valid ? item : 0;       // clamped so the index math below stays in range
+  const uint32_t token = div_groups.div(it);  // b * L + l
   const int g = static_cast<int>(it - token * groups);
-  const int l = static_cast<int>(token % L);
-  const int b = static_cast<int>(token / L);
+  const uint32_t b32 = div_L.div(token);
+  const int l = static_cast<int>(token - b32 * L);
+  const int b = static_cast<int>(b32);
   const int rows3 = 3 * H;
   const int col = lane16 * 8;
 
@@ -150,19 +172,21 @@ static int launch_rows(const uint16_t* qkv, const uint16_t* q_scale, const uint1
                        uint16_t* k, uint16_t* v, cudaStream_t stream) {
   const int groups = (3 * H + kRows - 1) / kRows;
   const long long n_items = static_cast<long long>(B) * L * groups;
+  if (n_items * 16 >= (1ll << 31)) return FLK_ERR_UNSUPPORTED;  // 32-bit thread indices in the kernel
   const long long blocks = (n_items * 16 + kThreads - 1) / kThreads;
-  if (blocks > 0x7FFFFFFFLL) return FLK_ERR_UNSUPPORTED;
   qk_prep_kernel<kRows, kMinBlocks><<<static_cast<unsigned>(blocks), kThreads, 0, stream>>>(
-      qkv, q_scale, k_scale, cos_t, sin_t, q_gain, L, H, groups, n_items, S_out, row0, q, k, v);
+      qkv, q_scale, k_scale, cos_t, sin_t, q_gain, L, H, groups, static_cast<uint32_t>(n_items),
+      make_fast_div(static_cast<uint32_t>(groups)), make_fast_div(static_cast<uint32_t>(L)), S_out, row0, q, k, v);
   return cudaGetLastError() == cudaSuccess ? FLK_OK : FLK_ERR_CUDA;
 }
 
 int launch_qk_prep(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t* k_scale, const float* cos_t,
                    const float* sin_t, float q_gain, int B, int L, int H, int S_out, int row0, uint16_t* q,
                    uint16_t* k, uint16_t* v, cudaStream_t stream) {
-  // 8 head rows per work item, 3 CTAs of 256 threads per SM (80 registers): the fastest of the
-  // {4, 6, 8} rows x {2..6} CTAs/SM configurations measured at the 1024^2 shape.
-  return launch_rows<8, 3>(qkv, q_scale, k_scale, cos_t, sin_t, q_gain, B, L, H, S_out, row0, q, k, v, stream);
+  // 4 head rows per work item, 4 CTAs of 256 threads per SM (64 registers, no spills): the fastest
+  // of the {2, 3, 4, 6, 8} rows x {2..8} CTAs/SM configurations measured at the 1024^2 shape
+  // (fewer rows or more CTAs spill; 8 rows x 3 CTAs is 6 % slower).
+  return launch_rows<4, 4>(qkv, q_scale, k_scale, cos_t, sin_t, q_gain, B, L, H, S_out, row0, q, k, v, stream);
 }
 
 }  // namespace flk
