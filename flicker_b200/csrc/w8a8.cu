@@ -228,6 +228,23 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // ------------------------------------------------------------------ activation quantisation
+// clamp(rint(x' / scale), -127, 127) without a division per element. With inv = rn(1 / scale),
+// r = rn(x' * inv) is within 2^-23 relative (|q| <= ~254 even for a subnormal scale: 3e-5
+// absolute) of the exact quotient q, and the correctly rounded quotient rn(q) within 1.5e-5 of
+// it, so the two round to the same integer unless r lies within 4.5e-5 of a half-integer (or
+// rn(q) is a tie). r is rounded to an integer (half to even) by adding 1.5 * 2^23, exact for
+// |r| < 2^22; within 2^-14 of a half-integer, or when r is not finite, the correctly rounded
+// quotient is computed and converted instead.
+__device__ __forceinline__ int quant_code(float xs, float scale, float inv) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23, bit pattern 0x4B400000
+  const float r = __fmul_rn(xs, inv);
+  const float t = __fadd_rn(r, kRound);
+  const float e = fabsf(__fsub_rn(r, __fsub_rn(t, kRound)));  // |r - rint(r)|, exact
+  const int q = (e < 0.5f - 6.103515625e-05f) ? __float_as_int(t) - 0x4B400000
+                                              : __float2int_rn(__fdiv_rn(xs, scale));
+  return max(-127, min(127, q));
+}
+
 // One warp per row: x' = float(x) * inv_smooth, absmax over the row, scale = absmax / 127,
 // q = clamp(rint(x' / scale), -127, 127). K % 8 == 0 (16-byte vectors).
 __global__ void __launch_bounds__(256) quantize_act_kernel(const uint16_t* __restrict__ x,
@@ -255,6 +272,7 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const uint16_t* __res
   float scale = __fdiv_rn(amax, 127.0f);
   if (!(scale > 0.f)) scale = 1.0f;
   if (lane == 0) x_scale[row] = scale;
+  const float inv = __frcp_rn(scale);
   int8_t* qr = xq + static_cast<size_t>(row) * K;
   for (int c = lane * 8; c < K; c += 256) {
     const uint4 v = *reinterpret_cast<const uint4*>(xr + c);
@@ -266,66 +284,71 @@ __global__ void __launch_bounds__(256) quantize_act_kernel(const uint16_t* __res
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const float xv = (j & 1) ? __uint_as_float(w[j >> 1] & 0xFFFF0000u) : __uint_as_float(w[j >> 1] << 16);
-      const int qv = max(-127, min(127, __float2int_rn(__fdiv_rn(__fmul_rn(xv, sv[j]), scale))));
+      const int qv = quant_code(__fmul_rn(xv, sv[j]), scale, inv);
       packed[j >> 2] |= (static_cast<uint32_t>(qv) & 0xFFu) << (8 * (j & 3));
     }
     *reinterpret_cast<uint2*>(qr + c) = make_uint2(packed[0], packed[1]);
   }
 }
 
-// Same arithmetic with the row held in registers: every load of the row is issued before any
-// math (kIters x 16 B per lane in flight), and the codes are computed from the registers.
+// Same arithmetic with one CTA of 128 threads per row held in registers (K <= 1024 * kIters):
+// every load of the row is issued before any math, the absmax is reduced across the CTA, and the
+// codes are computed from the registers. Many small CTAs per SM keep the loads of some rows in
+// flight while others compute.
+constexpr int kRowThreads = 128;
 template <int kIters>
-__global__ void __launch_bounds__(256) quantize_act_reg_kernel(const uint16_t* __restrict__ x,
-                                                               const float* __restrict__ inv_s, int M, int K,
-                                                               int8_t* __restrict__ xq,
-                                                               float* __restrict__ x_scale) {
-  const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (row >= M) return;  // whole warp leaves together
+__global__ void __launch_bounds__(kRowThreads) quantize_act_row_kernel(const uint16_t* __restrict__ x,
+                                                                      const float* __restrict__ inv_s, int K,
+                                                                      int8_t* __restrict__ xq,
+                                                                      float* __restrict__ x_scale) {
+  __shared__ float red[kRowThreads / 32];
+  const int row = blockIdx.x;
+  const int tid = threadIdx.x;
   const uint16_t* xr = x + static_cast<size_t>(row) * K;
   uint4 v[kIters];
 #pragma unroll
   for (int it = 0; it < kIters; ++it) {
-    const int c = lane * 8 + it * 256;
+    const int c = (it * kRowThreads + tid) * 8;
     v[it] = c < K ? *reinterpret_cast<const uint4*>(xr + c) : make_uint4(0, 0, 0, 0);
   }
+  float xs[kIters][8];
   float amax = 0.f;
 #pragma unroll
   for (int it = 0; it < kIters; ++it) {
-    const int c = lane * 8 + it * 256;
-    if (c >= K) break;
-    const float4 s0 = __ldg(reinterpret_cast<const float4*>(inv_s + c));
-    const float4 s1 = __ldg(reinterpret_cast<const float4*>(inv_s + c + 4));
+    const int c = (it * kRowThreads + tid) * 8;
+    float4 s0 = make_float4(0.f, 0.f, 0.f, 0.f), s1 = s0;
+    if (c < K) {
+      s0 = __ldg(reinterpret_cast<const float4*>(inv_s + c));
+      s1 = __ldg(reinterpret_cast<const float4*>(inv_s + c + 4));
+    }
     const uint32_t w[4] = {v[it].x, v[it].y, v[it].z, v[it].w};
     const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      amax = fmaxf(amax, fabsf(__fmul_rn(__uint_as_float(w[j] << 16), sv[2 * j])));
-      amax = fmaxf(amax, fabsf(__fmul_rn(__uint_as_float(w[j] & 0xFFFF0000u), sv[2 * j + 1])));
+    for (int j = 0; j < 8; ++j) {
+      const float xv = (j & 1) ? __uint_as_float(w[j >> 1] & 0xFFFF0000u) : __uint_as_float(w[j >> 1] << 16);
+      xs[it][j] = __fmul_rn(xv, sv[j]);
+      amax = fmaxf(amax, fabsf(xs[it][j]));
     }
   }
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  if ((tid & 31) == 0) red[tid >> 5] = amax;
+  __syncthreads();
+#pragma unroll
+  for (int w = 0; w < kRowThreads / 32; ++w) amax = fmaxf(amax, red[w]);
   float scale = __fdiv_rn(amax, 127.0f);
   if (!(scale > 0.f)) scale = 1.0f;
-  if (lane == 0) x_scale[row] = scale;
+  if (tid == 0) x_scale[row] = scale;
+  const float inv = __frcp_rn(scale);
   int8_t* qr = xq + static_cast<size_t>(row) * K;
 #pragma unroll
   for (int it = 0; it < kIters; ++it) {
-    const int c = lane * 8 + it * 256;
+    const int c = (it * kRowThreads + tid) * 8;
     if (c >= K) break;
-    const float4 s0 = __ldg(reinterpret_cast<const float4*>(inv_s + c));
-    const float4 s1 = __ldg(reinterpret_cast<const float4*>(inv_s + c + 4));
-    const uint32_t w[4] = {v[it].x, v[it].y, v[it].z, v[it].w};
-    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
     uint32_t packed[2] = {0u, 0u};
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float xv = (j & 1) ? __uint_as_float(w[j >> 1] & 0xFFFF0000u) : __uint_as_float(w[j >> 1] << 16);
-      const int qv = max(-127, min(127, __float2int_rn(__fdiv_rn(__fmul_rn(xv, sv[j]), scale))));
-      packed[j >> 2] |= (static_cast<uint32_t>(qv) & 0xFFu) << (8 * (j & 3));
-    }
+    for (int j = 0; j < 8; ++j)
+      packed[j >> 2] |= (static_cast<uint32_t>(quant_code(xs[it][j], scale, inv)) & 0xFFu) << (8 * (j & 3));
     *reinterpret_cast<uint2*>(qr + c) = make_uint2(packed[0], packed[1]);
   }
 }
@@ -396,17 +419,22 @@ int launch_w8a8_gemm(const int8_t* xq, const int8_t* wq, const float* x_scale, c
 
 int launch_quantize_act(const uint16_t* x, const float* inv_s, int M, int K, int8_t* xq, float* x_scale,
                         cudaStream_t stream) {
-  const long long threads = static_cast<long long>(M) * 32;
-  const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
-  // Rows up to 4096 wide are held in registers; wider rows take the two-pass kernel.
+  // Rows up to 4096 wide: one CTA per row, held in registers; wider rows take the two-pass
+  // kernel (one warp per row).
+  const unsigned rows = static_cast<unsigned>(M);
   if (K <= 1024)
-    quantize_act_reg_kernel<4><<<blocks, 256, 0, stream>>>(x, inv_s, M, K, xq, x_scale);
+    quantize_act_row_kernel<1><<<rows, kRowThreads, 0, stream>>>(x, inv_s, K, xq, x_scale);
   else if (K <= 2048)
-    quantize_act_reg_kernel<8><<<blocks, 256, 0, stream>>>(x, inv_s, M, K, xq, x_scale);
+    quantize_act_row_kernel<2><<<rows, kRowThreads, 0, stream>>>(x, inv_s, K, xq, x_scale);
+  else if (K <= 3072)
+    quantize_act_row_kernel<3><<<rows, kRowThreads, 0, stream>>>(x, inv_s, K, xq, x_scale);
   else if (K <= 4096)
-    quantize_act_reg_kernel<16><<<blocks, 256, 0, stream>>>(x, inv_s, M, K, xq, x_scale);
-  else
-    quantize_act_kernel<<<blocks, 256, 0, stream>>>(x, inv_s, M, K, xq, x_scale);
+    quantize_act_row_kernel<4><<<rows, kRowThreads, 0, stream>>>(x, inv_s, K, xq, x_scale);
+  else {
+    const long long threads = static_cast<long long>(M) * 32;
+    quantize_act_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(x, inv_s, M, K, xq,
+                                                                                        x_scale);
+  }
   return cudaGetLastError() == cudaSuccess ? FLK_OK : FLK_ERR_CUDA;
 }
 

@@ -93,7 +93,7 @@ def test_errors():
         w8a8.quantize_act(torch.zeros(4, 8, dtype=torch.bfloat16), torch.ones(8))
 
 
-@pytest.mark.parametrize("m,k", [(64, 8), (33, 1000), (17, 2056), (9, 4096), (5, 4104)])
+@pytest.mark.parametrize("m,k", [(64, 8), (33, 1000), (11, 1536), (17, 2056), (7, 3072), (9, 4096), (5, 4104)])
 def test_quantize_act_widths(m, k):
     """Every row-width branch of the activation quantiser (register-held rows and the two-pass kernel)."""
     rng = np.random.default_rng(k)
@@ -103,3 +103,28 @@ def test_quantize_act_widths(m, k):
     gq, gs = w8a8.quantize_act(to_device(x), to_device(inv_s))
     np.testing.assert_array_equal(gq.cpu().numpy(), want_q)
     np.testing.assert_array_equal(gs.cpu().numpy().view(np.uint32), want_s.view(np.uint32))
+
+
+def test_quantize_ties_and_near_ties():
+    """Quotients x'/scale exactly on, and a few ulps either side of, every half-integer k + 0.5:
+    the codes must still round half to even exactly as numpy's float32 division does."""
+    m, k = 6, 1024
+    rng = np.random.default_rng(5)
+    x = np.ones((m, k), dtype=np.float32).astype(SQ.BF16)
+    inv_s = np.empty((m, k), dtype=np.float32)
+    for r in range(m):
+        amax = np.float32(rng.uniform(0.01, 50.0))
+        scale = np.float32(amax / np.float32(127.0))
+        inv_s[r, 0] = amax  # x'[r, 0] = 1 * amax sets the row's absmax
+        for j in range(1, k):
+            target = np.float32((j % 127 + 0.5) * np.float64(scale))
+            step = (j // 127) % 7 - 3  # -3 .. 3 ulps around the tie
+            for _ in range(abs(step)):
+                target = np.nextafter(target, np.float32(np.inf if step > 0 else -np.inf), dtype=np.float32)
+            inv_s[r, j] = -target if j % 2 else target
+    # one inv_smooth vector per row: quantise each row on its own
+    for r in range(m):
+        want_q, want_s = SQ.quantize_act(x[r:r + 1], inv_s[r])
+        gq, gs = w8a8.quantize_act(to_device(x[r:r + 1]), to_device(inv_s[r]))
+        np.testing.assert_array_equal(gs.cpu().numpy().view(np.uint32), want_s.view(np.uint32))
+        np.testing.assert_array_equal(gq.cpu().numpy(), want_q)
