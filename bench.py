@@ -18,8 +18,11 @@ Multi-GPU (torchrun, one process per GPU, NCCL):
   --shard batch  (default) each rank runs its own batch element (config 2:
                  batch 8 over 8 GPUs, seed = rank); no data-path collective;
                  weak scaling.
-  --shard heads  one batch-1 call split by heads (24/N per rank), followed by
-                 an NCCL all-gather of the attention output; strong scaling.
+  --shard heads  one batch-1 call split by heads (24/N per rank); strong scaling.
+                 --gather peer (default): the attention epilogue stores each
+                 rank's heads, merged ([1, S, 24*128]), straight into every
+                 rank's output over NVLink (symmetric memory), then one barrier;
+                 --gather nccl: attend, then an NCCL all-gather of [1, 24/N, S, 128].
 
 --impl reference times the reference's plain-XLA path restated on the host
 cores (jax is not installable, see oracle/cpu_baseline.py) on the same config.
@@ -55,6 +58,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(GRIDS), default="1024")
     ap.add_argument("--shard", choices=["batch", "heads"], default="batch")
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
+                    help="--shard heads: epilogue stores into every rank's buffer, or an NCCL all-gather")
     ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end leg (default K/10)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-heads", type=int, default=4, help="heads in the CPU-baseline sample")
@@ -509,8 +514,12 @@ def main():
     bytes_local = qk_prep_bytes(1, s, heads_local)
 
     gathered = None
+    peer = None
     if args.shard == "heads" and world > 1:
-        gathered = torch.empty((world, 1, heads_local, s, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+        if args.gather == "peer":
+            peer = sharding.PeerOutput((1, s, heads_total * HEAD_DIM), dev, group)
+        else:
+            gathered = torch.empty((world, 1, heads_local, s, HEAD_DIM), dtype=torch.bfloat16, device=dev)
 
     def step(i, rec=None):
         qkv, qs, ks, freqs = sets[i % 2]
@@ -519,7 +528,10 @@ def main():
         q, k, v = fb.qk_prep(qkv, qs, ks, freqs, heads_local)
         if rec is not None:
             rec[1].record()
-        o = fb.attend(q, k, v)
+        if peer is not None:
+            o = sharding.attend_gather_heads(q, k, v, peer, h0, heads_total)
+        else:
+            o = fb.attend(q, k, v)
         if rec is not None:
             rec[2].record()
         if gathered is not None:
@@ -561,8 +573,11 @@ def main():
     h_qkv = qkv0.cpu().pin_memory()
     h_tab = [t.cpu().pin_memory() for t in (freqs0.cos, freqs0.sin)]
     h_sc = [t.cpu().pin_memory() for t in (qs0, ks0)]
-    h_out = torch.empty((1, heads_total if gathered is not None else heads_local, s, HEAD_DIM),
-                        dtype=torch.bfloat16).pin_memory()
+    if peer is not None:
+        h_out = torch.empty((1, s, heads_total * HEAD_DIM), dtype=torch.bfloat16).pin_memory()
+    else:
+        h_out = torch.empty((1, heads_total if gathered is not None else heads_local, s, HEAD_DIM),
+                            dtype=torch.bfloat16).pin_memory()
     d_qkv = torch.empty_like(qkv0)
     d_tab = [torch.empty_like(freqs0.cos), torch.empty_like(freqs0.sin)]
     d_sc = [torch.empty_like(qs0), torch.empty_like(ks0)]
@@ -572,6 +587,9 @@ def main():
         for d, h in zip(d_tab + d_sc, h_tab + h_sc):
             d.copy_(h, non_blocking=True)
         q, k, v = fb.qk_prep(d_qkv, d_sc[0], d_sc[1], fb.Freqs(d_tab[0], d_tab[1], freqs0.q_gain), heads_local)
+        if peer is not None:
+            h_out.copy_(sharding.attend_gather_heads(q, k, v, peer, h0, heads_total), non_blocking=True)
+            return
         o = fb.attend(q, k, v)
         if gathered is not None:
             sharding.gather_heads(o, gathered, group)
@@ -617,7 +635,9 @@ def main():
                 "workload": f"flicker {args.config}^2 attention call: qk_prep + attend",
                 "batch": world if (args.shard == "batch" and world > 1) else 1,
                 "seq_len": s, "heads": heads_total, "head_dim": HEAD_DIM,
-                "parallelism": (f"batch{world}" if args.shard == "batch" else f"heads{world}+allgather")
+                "parallelism": (f"batch{world}" if args.shard == "batch" else
+                                (f"heads{world}+peer-store gather (merged heads)" if peer is not None
+                                 else f"heads{world}+nccl allgather"))
                 if world > 1 else "single",
                 "l2": "2 alternating input sets; per-step footprint (qkv + q,k,v + o) > 126 MB L2",
             },
@@ -641,6 +661,7 @@ def main():
             "device_status": status,
         }
     if world > 1:
+        peer = None  # release the symmetric-memory buffers before the group goes away
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:

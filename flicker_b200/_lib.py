@@ -32,6 +32,8 @@ SIGNATURES = {
                                 _u16p, _u16p, _u16p, _int, _int, ctypes.c_void_p]),
     "flk_attend_merged": (_int, [_u16p, _u16p, _u16p, _int, _int, _int, _int, _u16p, ctypes.c_void_p,
                                  ctypes.c_size_t, ctypes.c_void_p]),
+    "flk_attend_gather": (_int, [_u16p, _u16p, _u16p, _int, _int, _int, _int, ctypes.POINTER(ctypes.c_void_p),
+                                 _int, _int, _int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "flk_attend": (_int, [_u16p, _u16p, _u16p, _int, _int, _int, _int, _u16p, ctypes.c_void_p,
                           ctypes.c_size_t, ctypes.c_void_p]),
     "flk_attend_workspace_size": (ctypes.c_size_t, [_int, _int, _int, _int]),

@@ -66,13 +66,25 @@ struct alignas(1024) Smem {
   int abort;
 };
 
+// Where the bf16 output rows go. Head-major [B, H, S, 128] (kernels.attend), or heads merged into
+// [B, S, H_out * 128] rows (merge_heads) with this call's head h at position h0 + h, written
+// into each of the n_out buffers: one buffer normally; this GPU's and every peer's output when a
+// head-sharded call gathers its heads by storing them straight into the peers' memory.
+constexpr int kMaxOuts = 8;
+struct OutLayout {
+  int merged;
+  int H;      // heads of this call
+  int H_out;  // heads per merged output row
+  int h0;     // first head of this call within a merged row
+  int n_out;
+  uint16_t* o[kMaxOuts];
+};
+
 struct Params {
   int S;          // sequence length (multiple of 128)
   int n_tiles;    // S / 128
   int n_splits;   // KV splits (gridDim.z); 1 = the CTA normalises and writes o itself
-  int H;          // heads (locates a row of o in the merged layout)
-  int merged;     // 0: o is [B, H, S, 128]; 1: o is [B, S, H*128] (heads merged, kernels.attend + merge_heads)
-  uint16_t* o;    // bf16 output in the layout above
+  OutLayout out;  // bf16 output
   float* acc;     // split > 1: [n_splits, B*H*S, 128] fp32 un-normalised partial P.V
   float* lsum;    // split > 1: [n_splits, B*H*S] fp32 partial row sums
   int* status;    // device status word
@@ -121,14 +133,27 @@ __device__ __forceinline__ void row_sum_chunk(const uint32_t (&pk)[16], float2& 
 // columns [64h, 64h+32), i.e. over S columns it has already read.
 __device__ __forceinline__ uint32_t p_col(int kc) { return static_cast<uint32_t>((kc >> 2) * 64 + (kc & 3) * 8); }
 
-// Row of o that holds query row `grow` (= (b * H + h) * S + s): itself in the head-major
-// [B, H, S, 128] layout; (b * S + s) * H + h when heads are merged into [B, S, H * 128]
-// (modules.merge_heads, src/flicker/modules.py:63-65).
-__device__ __forceinline__ size_t out_row(size_t grow, int S, int H, int merged) {
-  if (!merged) return grow;
+// 128-column output row that holds query row `grow` (= (b * H + h) * S + s): itself in the
+// head-major layout; (b * S + s) * H_out + h0 + h when heads are merged (modules.merge_heads,
+// src/flicker/modules.py:63-65).
+__device__ __forceinline__ size_t out_row(size_t grow, int S, const OutLayout& L) {
+  if (!L.merged) return grow;
   const size_t bh = grow / S, s = grow - bh * S;
-  const size_t b = bh / H, h = bh - b * H;
-  return (b * S + s) * H + h;
+  const size_t b = bh / L.H, h = bh - b * L.H;
+  return (b * S + s) * L.H_out + L.h0 + h;
+}
+
+// Stores 16 packed bf16x2 words (32 columns) at element offset `off` of every output buffer.
+// Stores into a peer GPU's buffer are followed by a system-scope fence so that they are
+// visible before whatever synchronisation the caller performs after the kernel.
+__device__ __forceinline__ void store_out(const OutLayout& L, size_t off, const uint32_t (&pk)[16]) {
+#pragma unroll 1
+  for (int d = 0; d < L.n_out; ++d) {
+    uint4* dst = reinterpret_cast<uint4*>(L.o[d] + off);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+  }
+  if (L.n_out > 1) __threadfence_system();
 }
 
 // Epilogue of one softmax warp: its 32 rows x 64 columns of O from TMEM, either normalised and
@@ -136,7 +161,7 @@ __device__ __forceinline__ size_t out_row(size_t grow, int S, int H, int merged)
 // Kept out of line so that this once-per-CTA code sits apart from the KV loop's code.
 __device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t grow, int half, int split, float l) {
   if (p.n_splits == 1) {
-    uint16_t* orow = p.o + out_row(grow, p.S, p.H, p.merged) * kDim + half * 64;
+    const size_t orow = out_row(grow, p.S, p.out) * kDim + half * 64;
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {
       uint32_t r[32];
@@ -146,9 +171,7 @@ __device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t
 #pragma unroll
       for (int i = 0; i < 16; ++i)
         pk[i] = pack_bf16x2(__fdiv_rn(__uint_as_float(r[2 * i]), l), __fdiv_rn(__uint_as_float(r[2 * i + 1]), l));
-      uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+      store_out(p.out, orow + c * 32, pk);
     }
   } else {
     // Partial result of this split: un-normalised fp32 accumulator and row sum.
@@ -169,7 +192,7 @@ __device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t
 
 __global__ void __launch_bounds__(kThreads, 1)
     attend_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, const Params p) {
+                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   Smem& sm = *smem_ptr(smem_raw);
   const int warp = threadIdx.x >> 5;
@@ -379,8 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // o = bf16(sum_s acc_s / sum_s l_s) over the KV splits; one thread per 8 output columns.
 __global__ void __launch_bounds__(256) combine_splits_kernel(const float* __restrict__ acc,
                                                              const float* __restrict__ lsum, int n_splits,
-                                                             long long rows, int S, int H, int merged,
-                                                             uint16_t* __restrict__ o) {
+                                                             long long rows, int S, const __grid_constant__ OutLayout L) {
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= rows * (kDim / 8)) return;
   const long long row = idx / (kDim / 8);
@@ -397,7 +419,10 @@ __global__ void __launch_bounds__(256) combine_splits_kernel(const float* __rest
   uint32_t pk[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) pk[i] = pack_bf16x2(__fdiv_rn(a[2 * i], l), __fdiv_rn(a[2 * i + 1], l));
-  *reinterpret_cast<uint4*>(o + out_row(row, S, H, merged) * kDim + col) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  const size_t off = out_row(row, S, L) * kDim + col;
+#pragma unroll 1
+  for (int d = 0; d < L.n_out; ++d) *reinterpret_cast<uint4*>(L.o[d] + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  if (L.n_out > 1) __threadfence_system();
 }
 
 }  // namespace
@@ -453,8 +478,8 @@ size_t attend_workspace_bytes(int B, int H, int S, int splits) {
   return splits * rows * (kDim + 1) * sizeof(float);
 }
 
-int launch_attend_layout(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, uint16_t* o,
-                         int merged, int splits, void* workspace, int* status, cudaStream_t stream) {
+int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S,
+                      const OutLayout& out, int splits, void* workspace, int* status, cudaStream_t stream) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return FLK_ERR_CUDA;
   static bool configured[64] = {};
@@ -473,9 +498,7 @@ int launch_attend_layout(const uint16_t* q, const uint16_t* k, const uint16_t* v
   p.S = S;
   p.n_tiles = S / kTile;
   p.n_splits = splits;
-  p.H = H;
-  p.merged = merged;
-  p.o = o;
+  p.out = out;
   p.acc = splits > 1 ? static_cast<float*>(workspace) : nullptr;
   p.lsum = splits > 1 ? p.acc + static_cast<size_t>(splits) * rows * kDim : nullptr;
   p.status = status;
@@ -485,10 +508,38 @@ int launch_attend_layout(const uint16_t* q, const uint16_t* k, const uint16_t* v
   if (splits > 1) {
     const long long threads = rows * (kDim / 8);
     combine_splits_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
-        p.acc, p.lsum, splits, rows, S, H, merged, o);
+        p.acc, p.lsum, splits, rows, S, out);
     if (cudaGetLastError() != cudaSuccess) return FLK_ERR_CUDA;
   }
   return FLK_OK;
+}
+
+int launch_attend_layout(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, uint16_t* o,
+                         int merged, int splits, void* workspace, int* status, cudaStream_t stream) {
+  OutLayout out{};
+  out.merged = merged;
+  out.H = H;
+  out.H_out = H;
+  out.h0 = 0;
+  out.n_out = 1;
+  out.o[0] = o;
+  return launch_attend_out(q, k, v, B, H, S, out, splits, workspace, status, stream);
+}
+
+// Merged rows of H_out heads, this call's heads at [h0, h0 + H), written into each of the
+// n_out buffers (this GPU's and peers' memory, all addressable from this device).
+int launch_attend_gather(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S,
+                         uint16_t* const* outs, int n_out, int H_out, int h0, int splits, void* workspace,
+                         int* status, cudaStream_t stream) {
+  if (n_out < 1 || n_out > kMaxOuts) return FLK_ERR_INVALID_ARGUMENT;
+  OutLayout out{};
+  out.merged = 1;
+  out.H = H;
+  out.H_out = H_out;
+  out.h0 = h0;
+  out.n_out = n_out;
+  for (int d = 0; d < n_out; ++d) out.o[d] = outs[d];
+  return launch_attend_out(q, k, v, B, H, S, out, splits, workspace, status, stream);
 }
 
 // Head-major output ([B, H, S, 128]), the layout of kernels.attend.

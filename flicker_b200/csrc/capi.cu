@@ -18,6 +18,9 @@ int launch_qk_prep(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t*
                    uint16_t* k, uint16_t* v, cudaStream_t stream);
 int launch_attend_layout(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, uint16_t* o,
                          int merged, int splits, void* workspace, int* status, cudaStream_t stream);
+int launch_attend_gather(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S,
+                         uint16_t* const* outs, int n_out, int H_out, int h0, int splits, void* workspace,
+                         int* status, cudaStream_t stream);
 int attend_splits(int B, int H, int S, int sms);
 size_t attend_workspace_bytes(int B, int H, int S, int splits);
 int launch_w8a8_gemm(const int8_t* xq, const int8_t* wq, const float* x_scale, const float* w_scale, int M, int N,
@@ -201,6 +204,34 @@ int flk_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, i
 int flk_attend_merged(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, int D,
                       uint16_t* o, void* workspace, size_t ws_bytes, void* stream) {
   return attend_entry(q, k, v, B, H, S, D, o, 1, workspace, ws_bytes, stream);
+}
+
+int flk_attend_gather(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, int D,
+                      uint16_t* const* outs, int n_outs, int H_total, int h0, void* workspace, size_t ws_bytes,
+                      void* stream) {
+  int err = FLK_OK;
+  if (!attend_shape_ok(B, H, S, D, &err)) return err;
+  if (outs == nullptr || n_outs < 1 || n_outs > 8) return FLK_ERR_INVALID_ARGUMENT;
+  if (h0 < 0 || H_total < 1 || static_cast<long long>(h0) + H > H_total) return FLK_ERR_INVALID_ARGUMENT;
+  if (static_cast<long long>(B) * S == 0) return FLK_OK;
+  const void* ptrs[] = {q, k, v};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return FLK_ERR_INVALID_ARGUMENT;
+  for (int d = 0; d < n_outs; ++d)
+    if (outs[d] == nullptr || !aligned16(outs[d])) return FLK_ERR_INVALID_ARGUMENT;
+  const DeviceState* st = device_state(&err);
+  if (!st) return err;
+  int splits = flk::attend_splits(B, H, S, st->sms);
+  if (splits > 1) {
+    const size_t need = flk::attend_workspace_bytes(B, H, S, splits);
+    if (workspace == nullptr && ws_bytes == 0) {
+      splits = 1;
+    } else if (workspace == nullptr || ws_bytes < need || !aligned16(workspace)) {
+      return FLK_ERR_WORKSPACE;
+    }
+  }
+  return flk::launch_attend_gather(q, k, v, B, H, S, outs, n_outs, H_total, h0, splits, workspace, st->status,
+                                   static_cast<cudaStream_t>(stream));
 }
 
 int flk_w8a8_quantize_act(const uint16_t* x, const float* inv_smooth, int M, int K, int8_t* xq, float* x_scale,

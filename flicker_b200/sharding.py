@@ -7,10 +7,13 @@ the hot path shards without any exchange inside it:
   exchanged -- each rank's output feeds its own downstream layers;
 * head sharding (batch 1): rank r owns heads [r*H/n, (r+1)*H/n). Its fused-QKV
   input holds only those heads' q, k and v columns (what a column-parallel QKV
-  projection produces), it runs qk_prep + attend locally, and one all-gather
-  assembles the [B, H, S, D] output that ``merge_heads`` needs.
+  projection produces), it runs qk_prep + attend locally, and the ranks' heads
+  are assembled either by one all-gather (``gather_heads``, then ``merge_heads``)
+  or by the attention epilogue itself (``attend_gather_heads``): every rank stores
+  its heads' merged rows straight into every rank's output buffer over NVLink
+  (``PeerOutput``, torch symmetric memory), followed by one barrier.
 
-The collective runs on whatever process group it is given: NCCL over NVLink on
+The all-gather runs on whatever process group it is given: NCCL over NVLink on
 the B200 box, gloo in the CPU tests of the layout logic.
 """
 from __future__ import annotations
@@ -63,3 +66,57 @@ def merge_heads(x: torch.Tensor) -> torch.Tensor:
     """src/flicker/modules.py:63-65: [B, H, N, D] -> [B, N, H*D]."""
     b, h, n, d = x.shape
     return x.transpose(1, 2).reshape(b, n, h * d)
+
+
+class PeerOutput:
+    """Merged-head output buffers [B, S, H_total * D] bf16 that every rank of ``group`` can store into.
+
+    Allocated from torch symmetric memory and exchanged once (a collective), so each rank holds
+    device pointers to all ranks' buffers (``ptrs``, in rank order). ``copies`` buffers are
+    kept and used in turn: a rank storing into buffer i of step n + copies knows every peer has
+    finished with that buffer's step-n contents, because it passed the barrier of step
+    n + 1 ... after them (each rank consumes its output in stream order before its next call).
+    """
+
+    def __init__(self, shape, device, group, copies: int = 2):
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.bufs, self.handles, self.ptrs = [], [], []
+        for _ in range(copies):
+            buf = symm_mem.empty(*shape, dtype=torch.bfloat16, device=device)
+            handle = symm_mem.rendezvous(buf, group)
+            self.bufs.append(buf)
+            self.handles.append(handle)
+            self.ptrs.append([int(p) for p in handle.buffer_ptrs])
+        self.turn = 0
+
+
+def attend_gather_heads(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, peer: PeerOutput, h0: int,
+                        num_heads: int) -> torch.Tensor:
+    """Head-sharded attention whose epilogue stores this rank's heads [h0, h0 + H) of the merged
+    rows into every rank's buffer; after the barrier, the returned local buffer holds
+    merge_heads(attend(q, k, v)) over all ``num_heads`` heads on every rank."""
+    import ctypes
+
+    from . import _lib, kernels
+
+    q, k, v, batch, heads, length, dim = kernels._attend_args(q, k, v, None)
+    i = peer.turn
+    peer.turn = (peer.turn + 1) % len(peer.bufs)
+    buf, handle, ptrs = peer.bufs[i], peer.handles[i], peer.ptrs[i]
+    if tuple(buf.shape) != (batch, length, num_heads * dim):
+        raise ValueError(f"peer buffer {tuple(buf.shape)} is not [B, S, H*D] = {(batch, length, num_heads * dim)}")
+    outs = (ctypes.c_void_p * len(ptrs))(*ptrs)
+    lib = _lib.lib()
+    with torch.cuda.device(q.device):
+        ws_bytes = lib.flk_attend_workspace_size(batch, heads, length, dim)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
+        code = lib.flk_attend_gather(q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, length, dim, outs,
+                                     len(ptrs), num_heads, h0, ws.data_ptr() if ws is not None else None,
+                                     ws_bytes, kernels._stream(q))
+    _lib.check("flk_attend_gather", code)
+    handle.barrier()
+    return buf

@@ -87,6 +87,22 @@ int flk_attend_merged(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                       int B, int H, int S, int D, uint16_t* o,
                       void* workspace, size_t ws_bytes, void* stream);
 
+/*
+ * flk_attend_merged for one shard of heads, gathered by its own stores: this call's H heads
+ * (q, k, v [B, H, S, D]) are heads [h0, h0 + H) of merged rows [B, S, H_total * D], and every
+ * output row is written into each of the n_outs (1..8) buffers outs[] (a host array of device
+ * pointers, all addressable from the current device: this GPU's output and peers' outputs
+ * mapped into this process). When every rank of a head-sharded call does this, each rank's
+ * buffer holds merge_heads of all H_total heads after the ranks synchronise, which replaces
+ * the all-gather after attention (ncclAllGather over [H/n, S, D] slabs) and the merge_heads
+ * transpose (src/flicker/modules.py:63-65,157). The kernel neither waits for peers nor signals
+ * them: the caller orders the buffers' use across ranks (a barrier after the call). Same
+ * workspace rules as flk_attend, for this call's B, H, S.
+ */
+int flk_attend_gather(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                      int B, int H, int S, int D, uint16_t* const* outs, int n_outs,
+                      int H_total, int h0, void* workspace, size_t ws_bytes, void* stream);
+
 /* Bytes of workspace flk_attend needs for this shape on the current device. */
 size_t flk_attend_workspace_size(int B, int H, int S, int D);
 

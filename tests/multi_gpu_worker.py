@@ -1,0 +1,63 @@
+"""One rank of the head-sharded attention call on a node (launched by tests/test_multi_gpu.py under
+torchrun, one process per GPU): qk_prep + attend on this rank's heads, gathered by the attention
+epilogue's stores into every rank's symmetric-memory buffer (sharding.attend_gather_heads), and,
+for comparison, by attend + an NCCL all-gather + merge_heads. Every rank checks, on two
+consecutive calls, that both gathers agree bit for bit and match the single-GPU result over all
+heads within the attention tolerance."""
+from __future__ import annotations
+
+import datetime
+import math
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+import flicker_b200 as fb  # noqa: E402
+from flicker_b200 import rope, sharding  # noqa: E402
+
+
+def main() -> int:
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dev = torch.device("cuda", int(os.environ["LOCAL_RANK"]))
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    H, num_txt, gh = 24, 512, 32
+    S = num_txt + gh * gh
+    h0, h1 = sharding.head_range(H, world, rank)
+    peer = sharding.PeerOutput((1, S, H * 128), dev, dist.group.WORLD)
+    gathered = torch.empty((world, 1, h1 - h0, S, 128), dtype=torch.bfloat16, device=dev)
+    ok = True
+    for step in range(2):
+        g = torch.Generator(device=dev)
+        g.manual_seed(step)  # same full input on every rank
+        qkv = torch.randn(1, S, 3 * H * 128, generator=g, device=dev).to(torch.bfloat16)
+        qs = (torch.rand(128, generator=g, device=dev) + 0.5).to(torch.bfloat16)
+        ks = (torch.rand(128, generator=g, device=dev) + 0.5).to(torch.bfloat16)
+        freqs = fb.lane_pair(rope.joint_pe(num_txt, gh, gh, device=dev), 1.0 / math.sqrt(128))
+        full = fb.attend_merged(*fb.qk_prep(qkv, qs, ks, freqs, H))
+        local = sharding.slice_qkv_heads(qkv, H, h0, h1).contiguous()
+        q, k, v = fb.qk_prep(local, qs, ks, freqs, h1 - h0)
+        fused = sharding.attend_gather_heads(q, k, v, peer, h0, H).clone()
+        o = fb.attend(q, k, v)
+        sharding.gather_heads(o, gathered, dist.group.WORLD)
+        nccl = sharding.merge_heads(gathered.view(1, H, S, 128))
+        torch.cuda.synchronize()
+        # the per-rank calls may run split over KV where the all-heads call does not, so they
+        # match it within the attention tolerance; both gathers carry the same per-rank results
+        same = bool(torch.equal(fused, nccl))
+        close = (fused.float() - full.float()).abs().max().item() <= 2e-2
+        ok &= same and close
+        print(f"rank {rank} step {step}: fused == nccl {same}, fused ~ full {close}", flush=True)
+    status = fb.device_status()
+    flag = torch.tensor([1 if (ok and status == 0) else 0], device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    del peer
+    dist.destroy_process_group()
+    return 0 if int(flag.item()) == 1 else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())

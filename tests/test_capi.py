@@ -108,6 +108,20 @@ def test_shape_checks_run_before_any_device_work():
                                 None) == _lib.FLK_ERR_UNSUPPORTED
     assert lib.flk_qk_prep_into(fake, fake, fake, fake, fake, 1.0, 1, 0, 2, 128, fake, fake, fake, 100, 100,
                                 None) == 0
+    # gathering attend: 1..8 outputs, heads [h0, h0 + H) inside H_total
+    outs = (ctypes.c_void_p * 9)(*([0x10000] * 9))
+    assert lib.flk_attend_gather(fake, fake, fake, 1, 2, 128, 128, outs, 0, 4, 0, None, 0, None) \
+        == _lib.FLK_ERR_INVALID_ARGUMENT
+    assert lib.flk_attend_gather(fake, fake, fake, 1, 2, 128, 128, outs, 9, 4, 0, None, 0, None) \
+        == _lib.FLK_ERR_INVALID_ARGUMENT
+    assert lib.flk_attend_gather(fake, fake, fake, 1, 2, 128, 128, outs, 2, 4, 3, None, 0, None) \
+        == _lib.FLK_ERR_INVALID_ARGUMENT
+    assert lib.flk_attend_gather(fake, fake, fake, 1, 2, 128, 128, None, 2, 4, 0, None, 0, None) \
+        == _lib.FLK_ERR_INVALID_ARGUMENT
+    odd_outs = (ctypes.c_void_p * 2)(0x10000, 0x10002)
+    assert lib.flk_attend_gather(fake, fake, fake, 1, 2, 128, 128, odd_outs, 2, 4, 0, None, 0, None) \
+        == _lib.FLK_ERR_INVALID_ARGUMENT
+    assert lib.flk_attend_gather(fake, fake, fake, 1, 2, 0, 128, outs, 2, 4, 0, None, 0, None) == 0
     # merged-heads attend: the same shape rules as flk_attend
     assert lib.flk_attend_merged(fake, fake, fake, 1, 2, 128, 64, fake, None, 0, None) == _lib.FLK_ERR_UNSUPPORTED
     assert lib.flk_attend_merged(fake, fake, fake, 1, 2, 100, 128, fake, None, 0, None) \

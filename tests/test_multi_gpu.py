@@ -1,0 +1,36 @@
+"""Head-sharded attention across two GPUs of one node (skipped on a box with fewer GPUs): the
+ranks' heads gathered by the attention epilogue's peer stores equal the NCCL all-gather of the
+same per-rank results and match the single-GPU call. Runs tests/multi_gpu_worker.py under torchrun, one process per GPU, inside
+a time limit so that a rank that stalls ends the run instead of hanging it."""
+from __future__ import annotations
+
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_head_sharded_gather_on_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs on this node")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr", "127.0.0.1", f"--master-port={free_port()}",
+           os.path.join(ROOT, "tests", "multi_gpu_worker.py")]
+    res = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True)
+    print(res.stdout[-3000:], res.stderr[-3000:])
+    assert res.returncode == 0
+    assert res.stdout.count("fused == nccl True, fused ~ full True") == 4
