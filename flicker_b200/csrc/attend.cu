@@ -144,8 +144,9 @@ __device__ __forceinline__ size_t out_row(size_t grow, int S, const OutLayout& L
 }
 
 // Stores 16 packed bf16x2 words (32 columns) at element offset `off` of every output buffer.
-// Stores into a peer GPU's buffer are followed by a system-scope fence so that they are
-// visible before whatever synchronisation the caller performs after the kernel.
+// A thread that stored into several buffers (peers' among them) ends its epilogue with one
+// system-scope fence, so that its stores are visible before whatever synchronisation the
+// caller performs after the kernel.
 __device__ __forceinline__ void store_out(const OutLayout& L, size_t off, const uint32_t (&pk)[16]) {
 #pragma unroll 1
   for (int d = 0; d < L.n_out; ++d) {
@@ -153,7 +154,6 @@ __device__ __forceinline__ void store_out(const OutLayout& L, size_t off, const 
 #pragma unroll
     for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
   }
-  if (L.n_out > 1) __threadfence_system();
 }
 
 // Epilogue of one softmax warp: its 32 rows x 64 columns of O from TMEM, either normalised and
@@ -173,6 +173,7 @@ __device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t
         pk[i] = pack_bf16x2(__fdiv_rn(__uint_as_float(r[2 * i]), l), __fdiv_rn(__uint_as_float(r[2 * i + 1]), l));
       store_out(p.out, orow + c * 32, pk);
     }
+    if (p.out.n_out > 1) __threadfence_system();
   } else {
     // Partial result of this split: un-normalised fp32 accumulator and row sum.
     const size_t plane = static_cast<size_t>(gridDim.y) * p.S;  // rows per split
