@@ -19,10 +19,11 @@ Multi-GPU (torchrun, one process per GPU, NCCL):
                  batch 8 over 8 GPUs, seed = rank); no data-path collective;
                  weak scaling.
   --shard heads  one batch-1 call split by heads (24/N per rank); strong scaling.
-                 --gather nccl (default): attend, then an NCCL all-gather of
-                 [1, 24/N, S, 128]; --gather peer: the attention epilogue stores
-                 each rank's heads, merged ([1, S, 24*128]), straight into every
-                 rank's output over NVLink (symmetric memory), then one barrier.
+                 --gather peer (default): the attention epilogue stores each
+                 rank's heads, merged ([1, S, 24*128]), straight into every
+                 rank's output over NVLink (TMA stores into symmetric memory),
+                 then one barrier; --gather nccl: attend, then an NCCL
+                 all-gather of [1, 24/N, S, 128].
 
 --impl reference times the reference's plain-XLA path restated on the host
 cores (jax is not installable, see oracle/cpu_baseline.py) on the same config.
@@ -58,7 +59,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(GRIDS), default="1024")
     ap.add_argument("--shard", choices=["batch", "heads"], default="batch")
-    ap.add_argument("--gather", choices=["nccl", "peer"], default="nccl",
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="--shard heads: epilogue stores into every rank's buffer, or an NCCL all-gather")
     ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end leg (default K/10)")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -85,6 +85,11 @@ struct Params {
   int n_tiles;    // S / 128
   int n_splits;   // KV splits (gridDim.z); 1 = the CTA normalises and writes o itself
   OutLayout out;  // bf16 output
+  // When a merged output goes to several buffers (a head-sharded call storing into its peers'
+  // outputs) and the CTA writes o itself: one TMA map per buffer over [B*S, H_out*128] bf16,
+  // 64-column x 32-row boxes with the 128-byte swizzle, so each warp's block leaves as one tile.
+  int tma_out;
+  CUtensorMap out_maps[kMaxOuts];
   float* acc;     // split > 1: [n_splits, B*H*S, 128] fp32 un-normalised partial P.V
   float* lsum;    // split > 1: [n_splits, B*H*S] fp32 partial row sums
   int* status;    // device status word
@@ -156,11 +161,55 @@ __device__ __forceinline__ void store_out(const OutLayout& L, size_t off, const 
   }
 }
 
+// Tiled TMA store of a shared-memory box into global memory (async proxy, bulk async-group).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int c0, int c1, const void* src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(smem_u32(src))
+               : "memory");
+}
+
 // Epilogue of one softmax warp: its 32 rows x 64 columns of O from TMEM, either normalised and
 // rounded to bf16 (o = bf16(acc / l), kernels.py:130) or, for a KV split, the fp32 partials.
-// Kept out of line so that this once-per-CTA code sits apart from the KV loop's code.
-__device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t grow, int half, int split, float l) {
-  if (p.n_splits == 1) {
+// Kept out of line so that this once-per-CTA code sits apart from the KV loop's code. `stage`
+// is this warp's 4 KB of shared memory (1024-byte aligned, free once the tile's MMAs are done).
+__device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t grow, int half, int split, float l,
+                                        uint8_t* stage) {
+  if (p.n_splits == 1 && p.tma_out) {
+    // Stage the 32 x 64 block in the 128-byte-swizzled layout the maps expect (16-byte unit j of
+    // row r at position j ^ (r & 7): conflict-free), then one lane stores it to every buffer.
+    const int lane = threadIdx.x & 31;
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(o_addr + c * 32, r);
+      tmem_wait_ld(r);
+      uint32_t pk[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        pk[i] = pack_bf16x2(__fdiv_rn(__uint_as_float(r[2 * i]), l), __fdiv_rn(__uint_as_float(r[2 * i + 1]), l));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int j = c * 4 + i;
+        *reinterpret_cast<uint4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+            make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncwarp();
+    if (lane == 0) {  // grow is the block's first query row here
+      const size_t bh = grow / p.S, s0 = grow - bh * p.S;
+      const size_t b = bh / p.out.H, h = bh - b * p.out.H;
+      const int x = static_cast<int>((p.out.h0 + h) * kDim + half * 64);
+      const int y = static_cast<int>(b * p.S + s0);
+#pragma unroll 1
+      for (int d = 0; d < p.out.n_out; ++d) tma_store_2d(&p.out_maps[d], x, y, stage);
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+      __threadfence_system();
+    }
+    __syncwarp();
+  } else if (p.n_splits == 1) {
     const size_t orow = out_row(grow, p.S, p.out) * kDim + half * 64;
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {
@@ -387,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t o_addr = tmem + lane_off + 256 + t * 128 + half * 64;
         const size_t grow = static_cast<size_t>(row_base) + (t0 + t) * kTile + row;  // global query row
-        store_rows(p, o_addr, grow, half, split, l);
+        store_rows(p, o_addr, grow, half, split, l, sm.q[t] + (sw % kSoftmaxWarps) * 4096);
       }
     }
   }
@@ -461,6 +510,19 @@ static bool make_tile_map(CUtensorMap* map, const void* base, long long rows) {
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Output map for the staged epilogue: [B*S rows, H_out*128 cols] bf16, 64 x 32 boxes, 128-byte swizzle.
+static bool make_out_map(CUtensorMap* map, const void* base, long long rows, int cols) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+  const cuuint32_t box[2] = {64, 32};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 static size_t attend_smem_bytes() { return sizeof(Smem) + 1024; }
 static_assert(sizeof(Smem) + 1024 <= 232448, "attend shared memory exceeds the 227 KB opt-in limit");
 
@@ -500,6 +562,11 @@ int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
   p.n_tiles = S / kTile;
   p.n_splits = splits;
   p.out = out;
+  p.tma_out = (out.merged && out.n_out > 1 && splits == 1) ? 1 : 0;
+  if (p.tma_out)
+    for (int d = 0; d < out.n_out; ++d)
+      if (!make_out_map(&p.out_maps[d], out.o[d], static_cast<long long>(B) * S, out.H_out * kDim))
+        return FLK_ERR_CUDA;
   p.acc = splits > 1 ? static_cast<float*>(workspace) : nullptr;
   p.lsum = splits > 1 ? p.acc + static_cast<size_t>(splits) * rows * kDim : nullptr;
   p.status = status;
