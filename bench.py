@@ -142,6 +142,65 @@ class ClockSampler:
         return False
 
 
+# ------------------------------------------------------------------ end-to-end leg
+class CopyPipeline:
+    """End-to-end steps through the public API with each step's copies inside the timed region.
+
+    Step i uploads its inputs (pinned host -> device input set i % 2) on an upload stream,
+    computes on the current stream and downloads its result (device -> pinned host buffer i % 2)
+    on a download stream, so one step's upload overlaps its neighbours' compute and download
+    (the two copy directions run at once). Every step still moves all of its own bytes.
+    """
+
+    def __init__(self, torch, host_inputs, out_shape, out_dtype):
+        self.torch = torch
+        self.host_inputs = host_inputs
+        self.up, self.down = torch.cuda.Stream(), torch.cuda.Stream()
+        self.dev = [[torch.empty_like(h, device="cuda") for h in host_inputs] for _ in range(2)]
+        self.host_out = [torch.empty(out_shape, dtype=out_dtype).pin_memory() for _ in range(2)]
+        self.used = [torch.cuda.Event() for _ in range(2)]   # compute of the last step on set k is done
+        self.loaded = [torch.cuda.Event() for _ in range(2)]  # upload into set k is done
+        self.h2d_bytes = sum(t.numel() * t.element_size() for t in host_inputs)
+        self.d2h_bytes = self.host_out[0].numel() * self.host_out[0].element_size()
+
+    def run(self, steps, compute, before=None, persistent_out=False):
+        """Time `steps` steps; `compute(device_inputs)` returns the step's device result.
+
+        ``persistent_out``: the result lives in a buffer that the next step writes again (a
+        gather target), so a step's compute waits until the previous result is downloaded.
+        """
+        torch = self.torch
+        comp = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        fetched = torch.cuda.Event()
+        torch.cuda.synchronize()
+        if before is not None:
+            before()
+        e0.record(self.up)
+        for i in range(steps):
+            k = i % 2
+            with torch.cuda.stream(self.up):
+                if i >= 2:
+                    self.up.wait_event(self.used[k])
+                for d, h in zip(self.dev[k], self.host_inputs):
+                    d.copy_(h, non_blocking=True)
+                self.loaded[k].record(self.up)
+            comp.wait_event(self.loaded[k])
+            if persistent_out and i >= 1:
+                comp.wait_event(fetched)
+            out = compute(self.dev[k])
+            self.used[k].record(comp)
+            self.down.wait_event(self.used[k])
+            with torch.cuda.stream(self.down):
+                if not persistent_out:
+                    out.record_stream(self.down)
+                self.host_out[k].copy_(out, non_blocking=True)
+                fetched.record(self.down)
+        e1.record(self.down)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+
 # ------------------------------------------------------------------ inputs
 def make_inputs(torch, config, batch, heads, seed, device):
     """Seeded synthetic inputs: qkv ~ N(0,1) bf16, scales ~ U(0.5,1.5) bf16, joint RoPE lane tables."""
@@ -258,22 +317,10 @@ def run_w8a8(args, rank, world):
     g_us = statistics.mean(e[1].elapsed_time(e[2]) for e in ev_q) * 1e3
     ops = 2.0 * M * N * K
     # end to end through the layer: X from pinned host memory, y back to pinned host memory
-    hx = sets[0].cpu().pin_memory()
-    hy = torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
-    dx = torch.empty_like(sets[0])
-    e2e_steps = max(3, steps // 10)
-    for _ in range(2):
-        dx.copy_(hx, non_blocking=True)
-        hy.copy_(layer(dx), non_blocking=True)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(e2e_steps):
-        dx.copy_(hx, non_blocking=True)
-        hy.copy_(layer(dx), non_blocking=True)
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    pipe = CopyPipeline(torch, [sets[0].cpu().pin_memory()], (M, N), torch.bfloat16)
+    e2e_steps = args.e2e_steps or max(3, steps // 10)
+    pipe.run(2, lambda d: layer(d[0]))
+    e2e_ms = pipe.run(e2e_steps, lambda d: layer(d[0]))
     pk, pk_kind = peaks()
     int8_peak = 2.0 * pk["bf16_tflops"]  # no measured int8 peak: twice the measured bf16 GEMM
     gemm_tops = ops / (g_us * 1e-6) / 1e12
@@ -290,8 +337,8 @@ def run_w8a8(args, rank, world):
         "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": int8_peak, "unit": "TOPS",
                      "frac": gemm_tops / int8_peak, "traffic": None, "kernel": "w8a8_gemm",
                      "peak_source": f"2 x {pk_kind} bf16 burst (no measured int8 peak); nominal dense int8 4500"},
-        "e2e": {"value": ops / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS", "h2d_bytes_per_step": M * K * 2,
-                "d2h_bytes_per_step": M * N * 2, "steps": e2e_steps, "ms_per_step": e2e_ms},
+        "e2e": {"value": ops / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS", "h2d_bytes_per_step": pipe.h2d_bytes,
+                "d2h_bytes_per_step": pipe.d2h_bytes, "steps": e2e_steps, "ms_per_step": e2e_ms},
         "gpu_launches": 2 * steps, "clocks": clocks.summary, "device_status": _lib.lib().flk_device_status(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -409,29 +456,23 @@ def run_double(args, rank, world):
     # end to end through the public API: both streams' qkv, tables and scales from pinned host
     # memory, the merged output back to pinned host memory
     txt0, img0, ts0, is0, fr0 = sets[0]
-    hosts = [t.cpu().pin_memory() for t in (txt0, img0, fr0.cos, fr0.sin, *ts0, *is0)]
-    devs = [torch.empty_like(t, device=dev) for t in hosts]
-    h_out = torch.empty((1, s, H * HEAD_DIM), dtype=torch.bfloat16).pin_memory()
+    pipe = CopyPipeline(torch, [t.cpu().pin_memory() for t in (txt0, img0, fr0.cos, fr0.sin, *ts0, *is0)],
+                        (1, s, H * HEAD_DIM), torch.bfloat16)
+    joint = [tuple(torch.empty((1, H, s, HEAD_DIM), dtype=torch.bfloat16, device=dev) for _ in range(3))
+             for _ in range(2)]
+    turn = [0]
 
-    def e2e_step():
-        for d, h in zip(devs, hosts):
-            d.copy_(h, non_blocking=True)
-        dt, di, dc, dsn, a, b, c, e = devs
-        fb.qk_prep_into(dt, a, b, fb.Freqs(dc[:NUM_TXT], dsn[:NUM_TXT], fr0.q_gain), H, (q, k, v), 0)
-        fb.qk_prep_into(di, c, e, fb.Freqs(dc[NUM_TXT:], dsn[NUM_TXT:], fr0.q_gain), H, (q, k, v), NUM_TXT)
-        h_out.copy_(fb.attend_merged(q, k, v), non_blocking=True)
+    def e2e_compute(d):
+        dt, di, dc, dsn, a, b, c, e = d
+        qkv_j = joint[turn[0] % 2]  # joint buffers alternate with the input sets
+        turn[0] += 1
+        fb.qk_prep_into(dt, a, b, fb.Freqs(dc[:NUM_TXT], dsn[:NUM_TXT], fr0.q_gain), H, qkv_j, 0)
+        fb.qk_prep_into(di, c, e, fb.Freqs(dc[NUM_TXT:], dsn[NUM_TXT:], fr0.q_gain), H, qkv_j, NUM_TXT)
+        return fb.attend_merged(*qkv_j)
 
     e2e_steps = args.e2e_steps or max(3, K // 10)
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    pipe.run(2, e2e_compute)
+    e2e_ms = pipe.run(e2e_steps, e2e_compute)
     pk, pk_kind = peaks()
     f = result["fused"]
     at_tflops = flops / (f["attend_us"] * 1e-6) / 1e12
@@ -456,8 +497,8 @@ def run_double(args, rank, world):
                      "frac": at_tflops / pk["bf16_tflops"], "traffic": None, "kernel": "attend (merged store)",
                      "peak_source": f"{pk_kind} bf16 burst (cuBLAS)"},
         "e2e": {"value": flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in hosts),
-                "d2h_bytes_per_step": h_out.numel() * 2, "steps": e2e_steps, "ms_per_step": e2e_ms},
+                "h2d_bytes_per_step": pipe.h2d_bytes, "d2h_bytes_per_step": pipe.d2h_bytes, "steps": e2e_steps,
+                "ms_per_step": e2e_ms},
         "gpu_launches": 3 * K, "clocks": f["clocks"], "device_status": status,
     }
     if world == 1 and not args.no_cpu_baseline:
@@ -571,52 +612,33 @@ def main():
     # ---- end-to-end leg: host buffers through the public API, copies inside the timed region
     e2e_steps = args.e2e_steps or max(3, K // 10)
     qkv0, qs0, ks0, freqs0 = sets[0]
-    h_qkv = qkv0.cpu().pin_memory()
-    h_tab = [t.cpu().pin_memory() for t in (freqs0.cos, freqs0.sin)]
-    h_sc = [t.cpu().pin_memory() for t in (qs0, ks0)]
+    host_in = [t.cpu().pin_memory() for t in (qkv0, freqs0.cos, freqs0.sin, qs0, ks0)]
     if peer is not None:
-        h_out = torch.empty((1, s, heads_total * HEAD_DIM), dtype=torch.bfloat16).pin_memory()
+        out_shape = (1, s, heads_total * HEAD_DIM)
     else:
-        h_out = torch.empty((1, heads_total if gathered is not None else heads_local, s, HEAD_DIM),
-                            dtype=torch.bfloat16).pin_memory()
-    d_qkv = torch.empty_like(qkv0)
-    d_tab = [torch.empty_like(freqs0.cos), torch.empty_like(freqs0.sin)]
-    d_sc = [torch.empty_like(qs0), torch.empty_like(ks0)]
+        out_shape = (1, heads_total if gathered is not None else heads_local, s, HEAD_DIM)
+    pipe = CopyPipeline(torch, host_in, out_shape, torch.bfloat16)
 
-    def e2e_step():
-        d_qkv.copy_(h_qkv, non_blocking=True)
-        for d, h in zip(d_tab + d_sc, h_tab + h_sc):
-            d.copy_(h, non_blocking=True)
-        q, k, v = fb.qk_prep(d_qkv, d_sc[0], d_sc[1], fb.Freqs(d_tab[0], d_tab[1], freqs0.q_gain), heads_local)
+    def e2e_compute(d):
+        d_qkv, d_cos, d_sin, d_qs, d_ks = d
+        q, k, v = fb.qk_prep(d_qkv, d_qs, d_ks, fb.Freqs(d_cos, d_sin, freqs0.q_gain), heads_local)
         if peer is not None:
-            h_out.copy_(sharding.attend_gather_heads(q, k, v, peer, h0, heads_total), non_blocking=True)
-            return
+            return sharding.attend_gather_heads(q, k, v, peer, h0, heads_total)
         o = fb.attend(q, k, v)
         if gathered is not None:
             sharding.gather_heads(o, gathered, group)
-            h_out.copy_(gathered.view(h_out.shape), non_blocking=True)
-        else:
-            h_out.copy_(o, non_blocking=True)
+            return gathered.view(out_shape)
+        return o
 
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(e2e_steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
+    persistent = peer is not None or gathered is not None
+    pipe.run(2, e2e_compute, persistent_out=persistent)
+    e2e_ms = pipe.run(e2e_steps, e2e_compute, before=(lambda: dist.barrier()) if world > 1 else None,
+                      persistent_out=persistent) * e2e_steps
     if world > 1:
         t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    h2d = h_qkv.numel() * 2 + sum(t.numel() * t.element_size() for t in h_tab + h_sc)
-    d2h = h_out.numel() * 2
+    h2d, d2h = pipe.h2d_bytes, pipe.d2h_bytes
 
     pk, pk_kind = peaks()
     total_flops = flops_local * world if (args.shard == "batch" or world == 1) else attend_flops(1, s, heads_total)
