@@ -7,15 +7,16 @@
 // tensor memory for the whole KV loop and is read exactly once, in the epilogue.
 //
 // One CTA owns two 128-row query tiles of one (batch, head) and walks all KV blocks
-// of 128 rows. Warp roles (576 threads, 1 CTA per SM):
-//   warp 0      TMA producer: Q tiles once, then K_j, V_j into a 5-slot ring of 32 KB slots
-//   warp 1      TMEM allocator + UMMA issuer
-//   warps 2-5   "softmax" for query tile 0, warps 6-9 for query tile 1: one thread per
-//               query row (TMEM lane), exp + bf16 round + row sum, P written back to TMEM,
-//               then the epilogue O / l -> bf16 -> global.
+// of 128 rows (or one KV split of them). Warp roles (576 threads, 1 CTA per SM):
+//   warp 0       TMA producer: Q tiles once, then K_j, V_j into a 4-slot ring of 32 KB slots
+//   warp 1       TMEM allocator + UMMA issuer
+//   warps 2-17   softmax: 8 warps per query tile, two per TMEM lane quadrant, each owning 64 of
+//                the 128 columns of its 32 rows: exp + bf16 round, P written back to TMEM in two
+//                32-column chunks (each handed to the issuer with one arrival per warp), row
+//                sums; then the epilogue O / l -> bf16 -> global (or fp32 partials for a split).
 // The producer and issuer warps run converged: all 32 lanes walk the loop and wait on the
-// barriers (sleeping try_wait), and lane 0 alone issues the TMA / UMMA / commit instructions
-// through predicated inline PTX.
+// barriers with one warp-wide vote per wait; lane 0 issues the TMA loads and elect.sync picks
+// the lane that issues each UMMA and commit.
 // TMEM (512 columns x 128 lanes, fp32): S_t at columns [128t, 128t+128) for t = 0, 1, with
 // P_t (bf16, two per column) written over the first 64 of them; O_t at [256+128t, ...).
 // Per KV block the issuer runs, in order:
