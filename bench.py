@@ -48,6 +48,11 @@ NUM_HEADS = 24
 HEAD_DIM = 128
 NUM_TXT = 512
 GRIDS = {"512": (32, 32), "1024": (64, 64), "2048": (128, 128)}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch from one ncu capture of
+# each kernel on a B200 at this bench's workload; the capture commands and the other counters are
+# in profiles/ (attend_1024.md, qk_prep_1024.md, w8a8_gemm_config4.md). Reported as the roofline's
+# `traffic` beside the algorithmic bytes; other configurations report null.
+NCU_TRAFFIC_BYTES = {"attend@1024": 95_354_880, "qk_prep@1024": 118_335_744, "w8a8_gemm@config4": 86_272_768}
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -335,7 +340,8 @@ def run_w8a8(args, rank, world):
         "kernels": {"quantize_act": {"us": q_us, "GB/s": (M * K * 3 + M * 4 + K * 4) / (q_us * 1e-6) / 1e9},
                     "w8a8_gemm": {"us": g_us, "TOPS": gemm_tops}},
         "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": int8_peak, "unit": "TOPS",
-                     "frac": gemm_tops / int8_peak, "traffic": None, "kernel": "w8a8_gemm",
+                     "frac": gemm_tops / int8_peak, "traffic": NCU_TRAFFIC_BYTES["w8a8_gemm@config4"],
+                     "traffic_source": "ncu capture, profiles/w8a8_gemm_config4.md", "kernel": "w8a8_gemm",
                      "peak_source": f"2 x {pk_kind} bf16 burst (no measured int8 peak); nominal dense int8 4500"},
         "e2e": {"value": ops / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS", "h2d_bytes_per_step": pipe.h2d_bytes,
                 "d2h_bytes_per_step": pipe.d2h_bytes, "steps": e2e_steps, "ms_per_step": e2e_ms},
@@ -641,6 +647,11 @@ def main():
     h2d, d2h = pipe.h2d_bytes, pipe.d2h_bytes
 
     pk, pk_kind = peaks()
+
+    def traffic(kernel):
+        # captured at the single-GPU 1024^2 call with all 24 heads only
+        return NCU_TRAFFIC_BYTES.get(f"{kernel}@{args.config}") if heads_local == NUM_HEADS else None
+
     total_flops = flops_local * world if (args.shard == "batch" or world == 1) else attend_flops(1, s, heads_total)
     value = total_flops * K / (elapsed_ms * 1e-3) / 1e12
     e2e_value = total_flops * e2e_steps / (e2e_ms * 1e-3) / 1e12
@@ -672,10 +683,10 @@ def main():
                            "frac_bf16_spec_2250": at_tflops / 2250.0},
             },
             "roofline": {"bound": "tensor", "achieved": at_tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                         "frac": at_tflops / pk["bf16_tflops"], "traffic": None,
+                         "frac": at_tflops / pk["bf16_tflops"], "traffic": traffic("attend"),
                          "peak_source": f"{pk_kind} bf16 burst (cuBLAS)", "kernel": "attend"},
             "roofline_qk_prep": {"bound": "hbm", "achieved": qk_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                                 "frac": qk_gbs / pk["hbm_gbs"], "traffic": None,
+                                 "frac": qk_gbs / pk["hbm_gbs"], "traffic": traffic("qk_prep"),
                                  "peak_source": f"{pk_kind} HBM copy"},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps, "ms_per_step": e2e_ms / e2e_steps},
