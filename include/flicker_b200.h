@@ -149,6 +149,14 @@ int flk_w8a8_gemm(const int8_t* xq, const int8_t* wq, const float* x_scale, cons
 /* The raw int32 accumulators c [M, N] = a [M, K] @ b [N, K]^T of the same kernel (verification). */
 int flk_i8_gemm_s32(const int8_t* a, const int8_t* b, int M, int N, int K, int32_t* c, void* stream);
 
+/*
+ * Self-test of the failure path (no counterpart in the reference): launches one warp that
+ * waits on an mbarrier nothing arrives at. The bounded wait gives up after its ~2 s limit,
+ * stores 0 in *result (a device int; 1 would mean the wait succeeded) and records
+ * FLK_ERR_DEVICE_TIMEOUT, which the next flk_device_status() returns; the context stays usable.
+ */
+int flk_selftest_wait_timeout(int* result, void* stream);
+
 /* Reads (and clears) the device-side status word of the current device: 0 or FLK_ERR_DEVICE_TIMEOUT.
  * Synchronises the device. */
 int flk_device_status(void);
