@@ -94,6 +94,16 @@ def attend_flops(b, s, h, d=HEAD_DIM):
     return 4.0 * b * h * s * s * d
 
 
+def exp_check(s, heads, at_ms, clocks):
+    """Secondary check of attend: exponentials per second vs the MUFU rate at the sampled clock."""
+    exps = float(heads) * s * s
+    mhz = clocks.get("sm_mhz") or 1965.0
+    mufu_per_s = 148 * 16 * mhz * 1e6
+    per_s = exps / (at_ms * 1e-3)
+    return {"per_call": exps, "per_s": per_s, "on_mufu": 0.75, "mufu_peak_per_s": mufu_per_s,
+            "mufu_frac": 0.75 * per_s / mufu_per_s}
+
+
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
     """nvidia-smi clock/throttle samples of one GPU while the timed region runs."""
@@ -607,8 +617,9 @@ def main():
         if world > 1:
             dist.barrier()
     elapsed_ms = start.elapsed_time(end)
-    qk_ms = statistics.mean(r[0].elapsed_time(r[1]) for r in recs)
-    at_ms = statistics.mean(r[1].elapsed_time(r[2]) for r in recs)
+    qk_all = [r[0].elapsed_time(r[1]) for r in recs]
+    at_all = [r[1].elapsed_time(r[2]) for r in recs]
+    qk_ms, at_ms = statistics.mean(qk_all), statistics.mean(at_all)
     if world > 1:
         t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -676,9 +687,14 @@ def main():
                 "l2": "2 alternating input sets; per-step footprint (qkv + q,k,v + o) > 126 MB L2",
             },
             "kernels": {
-                "qk_prep": {"us": qk_ms * 1e3, "GB/s": qk_gbs, "bytes": bytes_local,
+                "qk_prep": {"us": qk_ms * 1e3, "us_p50": statistics.median(qk_all) * 1e3, "GB/s": qk_gbs,
+                            "bytes": bytes_local,
                             "frac_hbm": qk_gbs / pk["hbm_gbs"]},
-                "attend": {"us": at_ms * 1e3, "TFLOP/s": at_tflops, "flops": flops_local,
+                "attend": {"us": at_ms * 1e3, "us_p50": statistics.median(at_all) * 1e3, "TFLOP/s": at_tflops,
+                           "flops": flops_local,
+                           # exponentials: B*H*S^2 per call; 3 of 4 on MUFU.EX2 (16 per clock per SM),
+                           # 1 of 4 on the FMA-pipe polynomial
+                           "exp": exp_check(s, heads_local, at_ms, clocks.summary),
                            "frac_bf16": at_tflops / pk["bf16_tflops"],
                            "frac_bf16_spec_2250": at_tflops / 2250.0},
             },
