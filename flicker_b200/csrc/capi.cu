@@ -22,6 +22,12 @@ int launch_attend_gather(const uint16_t* q, const uint16_t* k, const uint16_t* v
                          uint16_t* const* outs, int n_out, int H_out, int h0, int splits, void* workspace,
                          int* status, cudaStream_t stream);
 int attend_splits(int B, int H, int S, int sms);
+int launch_linear_bf16(const uint16_t* x, const uint16_t* wt, int M, int N, int K, uint16_t* y, int* status, int sms,
+                       cudaStream_t stream);
+int launch_linear_qk_prep(const uint16_t* x, const uint16_t* wt, int M, int N, int K, int L, int H,
+                          const uint16_t* q_scale, const uint16_t* k_scale, const float* cos_t, const float* sin_t,
+                          float q_gain, uint16_t* q, uint16_t* k, uint16_t* v, int S_out, int row0, uint16_t* rest,
+                          int* status, int sms, cudaStream_t stream);
 size_t attend_workspace_bytes(int B, int H, int S, int splits);
 int launch_w8a8_gemm(const int8_t* xq, const int8_t* wq, const float* x_scale, const float* w_scale, int M, int N,
                      int K, uint16_t* y, int32_t* acc_out, int* status, int sms, cudaStream_t stream);
@@ -232,6 +238,41 @@ int flk_attend_gather(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
   }
   return flk::launch_attend_gather(q, k, v, B, H, S, outs, n_outs, H_total, h0, splits, workspace, st->status,
                                    static_cast<cudaStream_t>(stream));
+}
+
+int flk_linear(const uint16_t* x, const uint16_t* wt, int M, int N, int K, uint16_t* y, void* stream) {
+  if (M < 0 || N < 0 || K <= 0 || K % 8 != 0) return FLK_ERR_INVALID_ARGUMENT;
+  if (static_cast<long long>(M) * N == 0) return FLK_OK;
+  const void* ptrs[] = {x, wt, y};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return FLK_ERR_INVALID_ARGUMENT;
+  int err = FLK_OK;
+  const DeviceState* st = device_state(&err);
+  if (!st) return err;
+  return flk::launch_linear_bf16(x, wt, M, N, K, y, st->status, st->sms, static_cast<cudaStream_t>(stream));
+}
+
+int flk_linear_qk_prep(const uint16_t* x, const uint16_t* wt, int M, int N, int K, const uint16_t* q_scale,
+                       const uint16_t* k_scale, const float* cos, const float* sin, float q_gain, int B, int L, int H,
+                       int D, uint16_t* q, uint16_t* k, uint16_t* v, int S_out, int row0, uint16_t* rest,
+                       void* stream) {
+  if (B < 0 || L < 0 || H <= 0 || K <= 0 || K % 8 != 0 || N < 0) return FLK_ERR_INVALID_ARGUMENT;
+  if (D != 128) return FLK_ERR_UNSUPPORTED;
+  if (static_cast<long long>(B) * L != M) return FLK_ERR_INVALID_ARGUMENT;
+  const long long n_qkv = 3ll * H * D;
+  if (N < n_qkv || (N > n_qkv && rest == nullptr)) return FLK_ERR_INVALID_ARGUMENT;
+  if (row0 < 0 || S_out < 0 || static_cast<long long>(row0) + L > S_out) return FLK_ERR_INVALID_ARGUMENT;
+  if (!std::isfinite(q_gain)) return FLK_ERR_INVALID_ARGUMENT;
+  if (static_cast<long long>(B) * L == 0) return FLK_OK;
+  const void* ptrs[] = {x, wt, q_scale, k_scale, cos, sin, q, k, v};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return FLK_ERR_INVALID_ARGUMENT;
+  if (rest != nullptr && !aligned16(rest)) return FLK_ERR_INVALID_ARGUMENT;
+  int err = FLK_OK;
+  const DeviceState* st = device_state(&err);
+  if (!st) return err;
+  return flk::launch_linear_qk_prep(x, wt, M, N, K, L, H, q_scale, k_scale, cos, sin, q_gain, q, k, v, S_out, row0,
+                                    rest, st->status, st->sms, static_cast<cudaStream_t>(stream));
 }
 
 int flk_w8a8_quantize_act(const uint16_t* x, const float* inv_smooth, int M, int K, int8_t* xq, float* x_scale,

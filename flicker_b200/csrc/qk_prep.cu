@@ -23,6 +23,7 @@
 #include <cstdint>
 
 #include "flicker_b200.h"
+#include "qk_math.cuh"
 
 namespace flk {
 
@@ -57,40 +58,6 @@ __device__ __forceinline__ uint4 ld_stream(const uint16_t* p) {
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                : "l"(p));
   return r;
-}
-
-// bf16 pair word (low half = even column) -> the two values as fp32.
-__device__ __forceinline__ float2 unpack(uint32_t w) {
-  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
-}
-__device__ __forceinline__ uint32_t pack(float2 v) {
-  __nv_bfloat162 b = __float22bfloat162_rn(v);
-  return *reinterpret_cast<uint32_t*>(&b);
-}
-__device__ __forceinline__ __nv_bfloat162 as_bf2(uint32_t w) { return *reinterpret_cast<__nv_bfloat162*>(&w); }
-__device__ __forceinline__ uint32_t as_u32(__nv_bfloat162 b) { return *reinterpret_cast<uint32_t*>(&b); }
-
-// One row of 8 columns (4 pair words) owned by this lane: RMSNorm -> bf16 -> * scale (bf16) ->
-// RoPE in fp32 -> (* gain) -> bf16. `ss` is the row's sum of squares (all 128 columns).
-__device__ __forceinline__ uint4 norm_rope(uint4 x, float ss, uint4 scale, const float2 (&c)[4],
-                                           const float2 (&sn)[4], float gain) {
-  // rsqrt(mean + eps) on the SFU (<= 2 ulp; lax.rsqrt's own ulps are not pinned by the reference).
-  const float inv = rsqrtf(ss * (1.0f / kHeadDim) + 1e-6f);
-  const float2 inv2 = make_float2(inv, inv);
-  const uint32_t xw[4] = {x.x, x.y, x.z, x.w};
-  const uint32_t sw[4] = {scale.x, scale.y, scale.z, scale.w};
-  uint32_t o[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    // bf16(x * inv), then the bf16 x bf16 scale multiply rounded to bf16 (exact product, one rounding).
-    const __nv_bfloat162 nb = __hmul2(__float22bfloat162_rn(__fmul2_rn(unpack(xw[j]), inv2)), as_bf2(sw[j]));
-    const float2 w = unpack(as_u32(nb));
-    // rotation c * w + s * swap(w) with separate roundings (no contraction), as the reference body.
-    float2 r = __fadd2_rn(__fmul2_rn(c[j], w), __fmul2_rn(sn[j], make_float2(w.y, w.x)));
-    if (gain != 1.0f) r = __fmul2_rn(r, make_float2(gain, gain));
-    o[j] = pack(r);
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 template <int kRows, int kMinBlocks>
@@ -145,21 +112,14 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
       *reinterpret_cast<uint4*>(v_out + dst) = x[i];
       continue;
     }
-    float2 s2 = make_float2(0.f, 0.f);
-    const uint32_t w[4] = {x[i].x, x[i].y, x[i].z, x[i].w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = unpack(w[j]);
-      s2 = __ffma2_rn(f, f, s2);  // squares of bf16 values are exact in fp32
-    }
     // Sum over this half-warp's 16 lanes (the two half-warps of a warp decide independently).
     const unsigned hmask = 0xFFFFu << (threadIdx.x & 16);
-    float ss = s2.x + s2.y;
+    float ss = qk_group_ss(x[i]);
     ss += __shfl_xor_sync(hmask, ss, 8, 16);
     ss += __shfl_xor_sync(hmask, ss, 4, 16);
     ss += __shfl_xor_sync(hmask, ss, 2, 16);
     ss += __shfl_xor_sync(hmask, ss, 1, 16);
-    const uint4 o = norm_rope(x[i], ss, kind == 0 ? qsv : ksv, cs, sn, kind == 0 ? q_gain : 1.0f);
+    const uint4 o = qk_norm_rope(x[i], ss, kind == 0 ? qsv : ksv, cs, sn, kind == 0 ? q_gain : 1.0f);
     *reinterpret_cast<uint4*>((kind == 0 ? q_out : k_out) + dst) = o;
   }
 }

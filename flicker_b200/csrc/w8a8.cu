@@ -8,7 +8,9 @@
 //   acc[i, n] = sum_k xq[i, k] * wq[n, k]                      (int32, exact)
 //   y[i, n]   = bf16(float(acc) * (scale_x[i] * scale_w[n]))
 //
-// GEMM structure (one CTA per SM, persistent over 128 x 256 output tiles):
+// Batches of at least 256 tokens run on the CTA-pair GEMM of gemm.cu (256 x 256 tiles over two
+// SMs, kind::i8, same epilogue arithmetic). Smaller batches use this file's single-CTA kernel
+// (one CTA per SM, persistent over 128 x 256 output tiles):
 //   warp 0     TMA producer: per K-block of 128 bytes, one 128x128 box of xq and one 256x128 box
 //              of wq (N-major, K contiguous) into a 4-stage ring (48 KB per stage, 128-byte swizzle);
 //   warp 1     TMEM allocator + UMMA issuer: 4 MMAs of 128x256x32 per stage into one of two
@@ -26,6 +28,9 @@
 #include "ptx.cuh"
 
 namespace flk {
+
+int launch_gemm_pair_i8(const int8_t* xq, const int8_t* wq, const float* x_scale, const float* w_scale, int M, int N,
+                        int K, uint16_t* y, int32_t* acc_out, int* status, int sms, cudaStream_t stream);
 
 namespace {
 
@@ -232,224 +237,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
-// ------------------------------------------------------------------ CTA-pair GEMM
-// The same GEMM with 256 x 256 output tiles computed by a cluster of two CTAs on two SMs
-// (tcgen05.mma.cta_group::2): CTA r of the pair loads rows [128r, 128r + 128) of the tile's xq
-// block and rows [128r, 128r + 128) of its wq block into its own shared memory; the even CTA
-// issues 256 x 256 x 32 MMAs that read both CTAs' halves, and CTA r's tensor memory receives
-// output rows [128r, 128r + 128) x all 256 columns. Per SM and K block that is 32 KB of operands
-// for 512 MMA cycles, against 48 KB for the single-CTA 128 x 256 tile, whose operand traffic
-// from L2 bounds it. Each CTA's loads signal the even CTA's barrier; the even CTA's commits
-// arrive on both CTAs' barriers (commit multicast, no TMA multicast anywhere); epilogue warps of
-// both CTAs hand the accumulator back to the even CTA's barrier.
-constexpr int kPairStages = 6;
-constexpr int kPairHalf = 128 * kBK;           // 16 KB: 128 rows x 128 K bytes
-constexpr int kPairStageBytes = 2 * kPairHalf;  // per CTA and stage: A half + B half
-constexpr uint32_t kIdescI8Pair = (2u << 4) | (1u << 7) | (1u << 10) | ((256u >> 3) << 17) | ((256u >> 4) << 24);
-
-struct alignas(1024) PairSmem {
-  uint8_t a[kPairStages][kPairHalf];
-  uint8_t b[kPairStages][kPairHalf];
-  uint64_t full[kPairStages];   // even CTA: both halves of the stage have landed (tx bytes of both CTAs)
-  uint64_t empty[kPairStages];  // both CTAs: the stage's MMAs are done (multicast commit)
-  uint64_t acc_full[2];         // both CTAs: accumulator buffer complete (multicast commit)
-  uint64_t acc_empty[2];        // even CTA: the 8 epilogue warps of the pair have read the buffer
-  uint64_t drain;
-  uint32_t tmem_base;
-  int abort;
-};
-
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-// Shared::cluster address of the variable at `p` in the cluster's CTA `rank`.
-__device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
-  uint32_t a;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
-  return a;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-// 2-D TMA load into this CTA's shared memory whose completion bytes go to the barrier at
-// `bar_cluster` (the even CTA's barrier of the pair).
-__device__ __forceinline__ void tma_load_2d_pair(void* dst, const void* tmap, int c0, int c1, uint32_t bar_cluster) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(bar_cluster)
-      : "memory");
-}
-__device__ __forceinline__ void umma_i8_pair_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                                  uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\t"
-      "setp.ne.b32 p, %3, 0;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %4, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(accumulate), "r"(kIdescI8Pair)
-      : "memory");
-}
-// Arrive on the barrier at this offset in both CTAs of the pair once the pair's MMAs issued so
-// far have completed.
-__device__ __forceinline__ void tc_commit_pair_both_warp(uint64_t* bar) {
-  asm volatile(
-      "{\n\t.reg .pred e;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}\n" ::
-          "r"(smem_u32(bar)),
-      "h"(static_cast<uint16_t>(3))
-      : "memory");
-}
-__device__ __forceinline__ void tc_commit_pair_own_warp(uint64_t* bar) {
-  asm volatile(
-      "{\n\t.reg .pred e;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(smem_u32(bar))
-      : "memory");
-}
-
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
-    w8a8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                          const __grid_constant__ GemmParams p) {
-  extern __shared__ uint8_t smem_raw[];
-  PairSmem& sm = *reinterpret_cast<PairSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                              ~static_cast<uintptr_t>(1023));
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_ctarank();  // 0: issues the pair's MMAs
-  const int pair = blockIdx.x >> 1, n_pairs = gridDim.x >> 1;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kPairStages; ++s) {
-      mbar_init(&sm.full[s], 1);
-      mbar_init(&sm.empty[s], 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&sm.acc_full[b], 1);
-      mbar_init(&sm.acc_empty[b], 8);  // 4 epilogue warps in each CTA of the pair
-    }
-    mbar_init(&sm.drain, 1);
-    sm.abort = 0;
-    fence_mbar_init();
-  }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&sm.tmem_base)),
-                 "r"(kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-  }
-  tc_fence_before();
-  cluster_sync_all();  // both CTAs' barriers initialised and TMEM allocated before any use
-  tc_fence_after();
-  const uint32_t tmem = sm.tmem_base;
-  volatile int* abort = &sm.abort;
-  const int n_tiles_n = (p.N + 255) / 256;
-  const int n_tiles = ((p.M + 255) / 256) * n_tiles_n;
-
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer (both CTAs)
-    const bool leader = lane == 0;
-    if (leader) {
-      tma_prefetch_desc(&tm_a);
-      tma_prefetch_desc(&tm_b);
-    }
-    int n = 0;
-    int issued[kPairStages] = {};
-    bool ok = true;
-    for (int tile = pair; ok && tile < n_tiles; tile += n_pairs) {
-      const int m0 = (tile / n_tiles_n) * 256 + 128 * static_cast<int>(rank);
-      const int nb0 = (tile % n_tiles_n) * 256 + 128 * static_cast<int>(rank);
-      for (int kb = 0; kb < p.k_blocks; ++kb, ++n) {
-        const int s = n % kPairStages, use = n / kPairStages;
-        if (use > 0 && !mbar_wait_warp(&sm.empty[s], (use - 1) & 1, abort, p.status)) {
-          ok = false;
-          break;
-        }
-        if (leader) {
-          const uint32_t full0 = mapa_shared(&sm.full[s], 0);
-          if (rank == 0) mbar_arrive_expect_tx(&sm.full[s], 2 * kPairStageBytes);
-          tma_load_2d_pair(sm.a[s], &tm_a, kb * kBK, m0, full0);
-          tma_load_2d_pair(sm.b[s], &tm_b, kb * kBK, nb0, full0);
-        }
-        issued[s] = use + 1;
-        __syncwarp();
-      }
-    }
-    // Never leave with a copy in flight: the even CTA waits (bounded) for the last fill of every
-    // stage, which covers both CTAs' copies into it; the odd CTA's copies are covered by the
-    // empty[] phases it waited for and by the final cluster barrier, which the even CTA reaches
-    // only after its MMAs (the consumers of those copies) have drained.
-    if (rank == 0)
-      for (int s = 0; s < kPairStages; ++s)
-        if (issued[s] > 0) mbar_wait_warp(&sm.full[s], (issued[s] - 1) & 1, abort, p.status);
-  } else if (warp == 1) {
-    if (rank == 0) {
-      // ---------------------------------------------------------------- UMMA issuer (even CTA)
-      int n = 0, local = 0;
-      bool ok = true;
-      for (int tile = pair; ok && tile < n_tiles; tile += n_pairs, ++local) {
-        const int buf = local & 1, use = local >> 1;
-        if (use > 0 && !mbar_wait_warp(&sm.acc_empty[buf], (use - 1) & 1, abort, p.status)) break;
-        tc_fence_after();
-        const uint32_t d = tmem + buf * 256;
-        for (int kb = 0; kb < p.k_blocks; ++kb, ++n) {
-          const int s = n % kPairStages;
-          if (!mbar_wait_warp(&sm.full[s], (n / kPairStages) & 1, abort, p.status)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < kBK / 32; ++kk)
-            umma_i8_pair_warp(d, desc_k(sm.a[s], kk), desc_k(sm.b[s], kk), (kb > 0 || kk > 0) ? 1u : 0u);
-          tc_commit_pair_both_warp(&sm.empty[s]);  // the stage is free in both CTAs once read
-        }
-        if (ok) tc_commit_pair_both_warp(&sm.acc_full[buf]);
-      }
-      tc_commit_pair_own_warp(&sm.drain);
-      mbar_wait_warp(&sm.drain, 0, abort, p.status);
-    }
-  } else {
-    // -------------------------------------------------------------------- epilogue (both CTAs)
-    const int quad = warp & 3;
-    const int row_in_half = quad * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    const uint32_t acc_empty0[2] = {mapa_shared(&sm.acc_empty[0], 0), mapa_shared(&sm.acc_empty[1], 0)};
-    int local = 0;
-    for (int tile = pair; tile < n_tiles; tile += n_pairs, ++local) {
-      const int buf = local & 1, use = local >> 1;
-      if (!mbar_wait_warp(&sm.acc_full[buf], use & 1, abort, p.status)) break;
-      tc_fence_after();
-      const int row = (tile / n_tiles_n) * 256 + 128 * static_cast<int>(rank) + row_in_half;
-      const int n0 = (tile % n_tiles_n) * 256;
-      const bool row_ok = row < p.M;
-      const float sx = (row_ok && p.x_scale) ? p.x_scale[row] : 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 8; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem + lane_off + buf * 256 + c * 32, r);
-        tmem_wait_ld(r);
-        store_chunk(p, r, row, row_ok, n0 + c * 32, sx);
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(acc_empty0[buf]);
-    }
-  }
-
-  tc_fence_before();
-  cluster_sync_all();  // the even CTA's MMAs have drained; no CTA reads the other's memory after this
-  if (warp == 1) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
-  }
-}
-
 // ------------------------------------------------------------------ activation quantisation
 // clamp(rint(x' / scale), -127, 127) without a division per element. With inv = rn(1 / scale),
 // r = rn(x' * inv) is within 2^-23 relative (|q| <= ~254 even for a subnormal scale: 3e-5
@@ -626,32 +413,13 @@ static int launch_w8a8_gemm_single(const CUtensorMap& ma, const CUtensorMap& mb,
   return cudaGetLastError() == cudaSuccess ? FLK_OK : FLK_ERR_CUDA;
 }
 
-static int launch_w8a8_gemm_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmParams& p, int sms,
-                                 cudaStream_t stream) {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FLK_ERR_CUDA;
-  static bool configured[64] = {};
-  const size_t smem = sizeof(PairSmem) + 1024;
-  if (!configured[dev]) {
-    if (cudaFuncSetAttribute(w8a8_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
-      return FLK_ERR_CUDA;
-    configured[dev] = true;
-  }
-  const int pair_tiles = ((p.M + 255) / 256) * ((p.N + 255) / 256);
-  const int pairs = std::max(1, std::min(pair_tiles, sms / 2));
-  w8a8_gemm_pair_kernel<<<2 * pairs, kGemmThreads, smem, stream>>>(ma, mb, p);
-  return cudaGetLastError() == cudaSuccess ? FLK_OK : FLK_ERR_CUDA;
-}
-
 int launch_w8a8_gemm(const int8_t* xq, const int8_t* wq, const float* x_scale, const float* w_scale, int M, int N,
                      int K, uint16_t* y, int32_t* acc_out, int* status, int sms, cudaStream_t stream) {
   // Batches of at least 256 tokens run on CTA pairs (256 x 256 tiles); smaller ones on single
   // CTAs (128 x 256 tiles), where half of a pair's tile would be padding.
-  const bool pair = M >= 256;
+  if (M >= 256) return launch_gemm_pair_i8(xq, wq, x_scale, w_scale, M, N, K, y, acc_out, status, sms, stream);
   CUtensorMap ma, mb;
-  if (!make_i8_map(&ma, xq, M, K, pair ? 128 : kBM) || !make_i8_map(&mb, wq, N, K, pair ? 128 : kBN))
-    return FLK_ERR_CUDA;
+  if (!make_i8_map(&ma, xq, M, K, kBM) || !make_i8_map(&mb, wq, N, K, kBN)) return FLK_ERR_CUDA;
   GemmParams p;
   p.M = M;
   p.N = N;
@@ -664,7 +432,7 @@ int launch_w8a8_gemm(const int8_t* xq, const int8_t* wq, const float* x_scale, c
   p.y = y;
   p.acc_out = acc_out;
   p.status = status;
-  return pair ? launch_w8a8_gemm_pair(ma, mb, p, sms, stream) : launch_w8a8_gemm_single(ma, mb, p, sms, stream);
+  return launch_w8a8_gemm_single(ma, mb, p, sms, stream);
 }
 
 int launch_quantize_act(const uint16_t* x, const float* inv_s, int M, int K, int8_t* xq, float* x_scale,
@@ -689,6 +457,5 @@ int launch_quantize_act(const uint16_t* x, const float* inv_s, int M, int K, int
 }
 
 static_assert(sizeof(GemmSmem) + 1024 <= 232448, "w8a8 shared memory exceeds the 227 KB opt-in limit");
-static_assert(sizeof(PairSmem) + 1024 <= 232448, "w8a8 pair shared memory exceeds the 227 KB opt-in limit");
 
 }  // namespace flk

@@ -128,6 +128,28 @@ int flk_attend_noalloc(const uint16_t* q, const uint16_t* k, const uint16_t* v,
 int flk_logit_bound(const float* q_scale, const float* k_scale, int D, float* bound);
 
 /*
+ * linear: y[M, N] = bf16(x[M, K] @ w[K, N]) with fp32 accumulation on the bf16 tensor cores,
+ * the weights given transposed (wt = w^T, [N, K], K contiguous; prepared once at load).
+ * Replaces nn.linear (src/flicker/nn.py:13-14) on the QKV path. K % 8 == 0; pointers 16-byte
+ * aligned.
+ */
+int flk_linear(const uint16_t* x, const uint16_t* wt, int M, int N, int K, uint16_t* y, void* stream);
+
+/*
+ * The QKV projection with qk_prep fused into its epilogue: equals flk_linear(x, wt) followed by
+ * flk_qk_prep_into on its first 3*H*D columns, bit for bit, without writing the qkv block to
+ * memory. x [B*L, K] (M = B*L tokens), wt [N, K] with N >= 3*H*D; q, k, v [B, H, S_out, D]
+ * receive rows [row0, row0 + L); columns [3*H*D, N) (a single block's mlp part) go to rest
+ * [M, N - 3*H*D] bf16 (NULL allowed when N == 3*H*D). cos, sin [L, D] fp32; scales [D] bf16.
+ * Replaces linear + qkv_prep in modules.double_prepare_qkv / single_prepare_qkv
+ * (src/flicker/modules.py:127-134,184-190).
+ */
+int flk_linear_qk_prep(const uint16_t* x, const uint16_t* wt, int M, int N, int K,
+                       const uint16_t* q_scale, const uint16_t* k_scale, const float* cos, const float* sin,
+                       float q_gain, int B, int L, int H, int D, uint16_t* q, uint16_t* k, uint16_t* v,
+                       int S_out, int row0, uint16_t* rest, void* stream);
+
+/*
  * W8A8 SmoothQuant linear, step 1 (per token). No counterpart in the reference (flicker's linear
  * is a bf16 x @ w, src/flicker/nn.py:13-14); arithmetic per SmoothQuant (Xiao et al., 2022):
  *   x'[i,k] = float(x[i,k]) * inv_smooth[k];  x_scale[i] = max_k |x'[i,k]| / 127 (1 if 0);
