@@ -69,9 +69,10 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end leg (default K/10)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-heads", type=int, default=4, help="heads in the CPU-baseline sample")
-    ap.add_argument("--workload", choices=["attention", "w8a8", "double"], default="attention",
+    ap.add_argument("--workload", choices=["attention", "w8a8", "double", "projection"], default="attention",
                     help="attention: qk_prep + attend (the headline); w8a8: the SmoothQuant linear of config 4; "
-                         "double: a double block's attention section with the fused concat and merged heads")
+                         "double: a double block's attention section with the fused concat and merged heads; "
+                         "projection: the QKV projection GEMM with qk_prep fused into its epilogue")
     return ap.parse_args()
 
 
@@ -526,6 +527,121 @@ def run_double(args, rank, world):
     return 0
 
 
+# ------------------------------------------------------------------ fused QKV projection
+def run_projection(args, rank, world):
+    """One step = the 1024^2 call's QKV projection, x [4608, 3072] @ w [3072, 9216] (bf16, fp32
+    accumulation), with qk_prep fused into the GEMM's epilogue, writing q, k, v head-major. The
+    unfused composition (linear to a qkv buffer, then qk_prep) is timed beside it. Rank 0 only."""
+    if rank != 0:
+        return 0
+    import torch
+
+    import flicker_b200 as fb
+    from flicker_b200 import _lib, projection
+
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    H, K = NUM_HEADS, 3072
+    sets = []
+    for i in range(2):
+        qkv_unused, qs, ks, freqs = make_inputs(torch, args.config, 1, H, 100 * i, dev)
+        s = qkv_unused.shape[1]
+        del qkv_unused
+        g = torch.Generator(device=dev)
+        g.manual_seed(100 * i + 5)
+        x = torch.randn((1, s, K), generator=g, device=dev).to(torch.bfloat16)
+        sets.append((x, qs, ks, freqs))
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    w = (torch.randn((K, 3 * H * HEAD_DIM), generator=g, device=dev) / math.sqrt(K)).to(torch.bfloat16)
+    wt = projection.prepare_weight(w)
+    M, N = s, 3 * H * HEAD_DIM
+    ops = 2.0 * M * N * K
+
+    def fused(i, rec=None):
+        x, qs, ks, freqs = sets[i % 2]
+        if rec is not None:
+            rec[0].record()
+        out = projection.qkv_projection(x, wt, qs, ks, freqs, H)
+        if rec is not None:
+            rec[1].record()
+            rec[2].record()
+        return out[:3]
+
+    def unfused(i, rec=None):
+        x, qs, ks, freqs = sets[i % 2]
+        if rec is not None:
+            rec[0].record()
+        qkv = projection.linear(x, wt)
+        if rec is not None:
+            rec[1].record()
+        out = fb.qk_prep(qkv, qs, ks, freqs, H)
+        if rec is not None:
+            rec[2].record()
+        return out
+
+    a, b = fused(0), unfused(0)
+    torch.cuda.synchronize()
+    if not all(torch.equal(x, y) for x, y in zip(a, b)):
+        raise RuntimeError("fused and unfused projections differ")
+    K_steps = args.steps
+    result = {}
+    for name, fn in (("unfused", unfused), ("fused", fused)):
+        for i in range(max(3, args.warmup)):
+            fn(i)
+        recs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K_steps)]
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local_rank) as clocks:
+            torch.cuda.synchronize()
+            start.record()
+            for i in range(K_steps):
+                fn(i, recs[i])
+            end.record()
+            torch.cuda.synchronize()
+        result[name] = {"ms": start.elapsed_time(end) / K_steps,
+                        "gemm_us": statistics.mean(r[0].elapsed_time(r[1]) for r in recs) * 1e3,
+                        "qk_prep_us": statistics.mean(r[1].elapsed_time(r[2]) for r in recs) * 1e3,
+                        "clocks": clocks.summary}
+    status = _lib.lib().flk_device_status()
+    x0, qs0, ks0, fr0 = sets[0]
+    pipe = CopyPipeline(torch, [t.cpu().pin_memory() for t in (x0, fr0.cos, fr0.sin, qs0, ks0)], (3, 1, H, M, HEAD_DIM),
+                        torch.bfloat16)
+
+    def e2e_compute(d):
+        dx, dc, dsn, dqs, dks = d
+        o = torch.empty((3, 1, H, M, HEAD_DIM), dtype=torch.bfloat16, device=dev)  # q, k, v in one buffer
+        projection.qkv_projection(dx, wt, dqs, dks, fb.Freqs(dc, dsn, fr0.q_gain), H, out=(o[0], o[1], o[2]))
+        return o
+
+    e2e_steps = args.e2e_steps or max(3, K_steps // 10)
+    pipe.run(2, e2e_compute)
+    e2e_ms = pipe.run(e2e_steps, e2e_compute)
+    pk, pk_kind = peaks()
+    f = result["fused"]
+    tflops = ops / (f["gemm_us"] * 1e-6) / 1e12
+    line = {
+        "metric": f"QKV projection + qk_prep TFLOP/s @[{M}x{K}]x[{K}x{N}] (1024^2 call, bf16, qk_prep fused)",
+        "value": ops / (f["ms"] * 1e-3) / 1e12, "unit": "TFLOP/s", "n_gpus": 1, "steps": K_steps,
+        "warmup": max(3, args.warmup), "ms_per_step": f["ms"], "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "QKV projection (x @ w) with qk_prep in the GEMM epilogue", "M": M, "K": K, "N": N,
+                   "heads": H, "l2": "2 alternating input sets; weights (56.6 MB) L2-resident as in a real layer"},
+        "kernels": {"linear_qk_prep": {"us": f["gemm_us"], "TFLOP/s": tflops}},
+        "unfused": {"ms_per_step": result["unfused"]["ms"], "linear_us": result["unfused"]["gemm_us"],
+                    "qk_prep_us": result["unfused"]["qk_prep_us"],
+                    "speedup_fused": result["unfused"]["ms"] / f["ms"]},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": tflops / pk["bf16_tflops"], "traffic": None, "kernel": "gemm_pair_kernel (QK_PREP)",
+                     "peak_source": f"{pk_kind} bf16 burst (cuBLAS)"},
+        "e2e": {"value": ops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": pipe.h2d_bytes,
+                "d2h_bytes_per_step": pipe.d2h_bytes, "steps": e2e_steps, "ms_per_step": e2e_ms},
+        "gpu_launches": K_steps, "clocks": f["clocks"], "device_status": status,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 # ------------------------------------------------------------------ our arm
 def main():
     args = parse_args()
@@ -538,6 +654,8 @@ def main():
         return run_w8a8(args, rank, world)
     if args.workload == "double":
         return run_double(args, rank, world)
+    if args.workload == "projection":
+        return run_projection(args, rank, world)
 
     import datetime
 
