@@ -280,6 +280,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  // Launched as a programmatic dependent of the previous kernel in the stream (normally qk_prep):
+  // the set-up above overlaps that kernel's tail, and no thread touches global memory before the
+  // previous kernel has completed and its writes are visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   volatile int* abort = &sm.abort;
 
   if (warp == 0) {
@@ -572,7 +576,17 @@ int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
   p.lsum = splits > 1 ? p.acc + static_cast<size_t>(splits) * rows * kDim : nullptr;
   p.status = status;
   const dim3 grid((p.n_tiles + 1) / 2, B * H, splits);
-  attend_kernel<<<grid, kThreads, attend_smem_bytes(), stream>>>(mq, mk, mv, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = attend_smem_bytes();
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, attend_kernel, mq, mk, mv, p) != cudaSuccess) return FLK_ERR_CUDA;
   if (cudaGetLastError() != cudaSuccess) return FLK_ERR_CUDA;
   if (splits > 1) {
     const long long threads = rows * (kDim / 8);

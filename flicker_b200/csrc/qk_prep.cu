@@ -68,6 +68,9 @@ __global__ void __launch_bounds__(kThreads, kMinBlocks)
                    FastDiv div_groups, FastDiv div_L, int S_out, int row0, uint16_t* __restrict__ q_out,
                    uint16_t* __restrict__ k_out, uint16_t* __restrict__ v_out) {
   // 32-bit index math throughout (the host keeps 16 * n_items below 2^31).
+  // Let the next kernel in the stream (attend, launched as a programmatic dependent) start its
+  // set-up on SMs this grid frees; it waits for this grid's completion before reading q, k, v.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const uint32_t item = (blockIdx.x * kThreads + threadIdx.x) >> 4;
   const int lane16 = threadIdx.x & 15;
   const bool valid = item < n_items;
