@@ -62,7 +62,10 @@ struct alignas(1024) Smem {
   uint64_t p_part[2][2];  // [tile][column chunk]: P chunk c of every softmax warp of the tile is in TMEM
   uint64_t o_full[2];
   uint64_t drain;
-  float l_part[2][2][kTile];  // [tile][column half][row]: row sums of the two halves
+  // [item parity][tile][column half][row]: row sums of the two column halves. Two copies, so that
+  // a persistent CTA's warp writing the next item's sum cannot overtake its partner warp's read
+  // of the current one.
+  float l_part[2][2][2][kTile];
   uint32_t tmem_base;
   int abort;
 };
@@ -84,7 +87,10 @@ struct OutLayout {
 struct Params {
   int S;          // sequence length (multiple of 128)
   int n_tiles;    // S / 128
-  int n_splits;   // KV splits (gridDim.z); 1 = the CTA normalises and writes o itself
+  int n_splits;   // KV splits; 1 = the CTA normalises and writes o itself
+  int BH;         // batch x heads
+  int n_pairs;    // (n_tiles + 1) / 2 query-tile pairs per (batch, head)
+  int n_items;    // BH * n_pairs * n_splits work items (persistent kernel)
   OutLayout out;  // bf16 output
   // When a merged output goes to several buffers (a head-sharded call storing into its peers'
   // outputs) and the CTA writes o itself: one TMA map per buffer over [B*S, H_out*128] bf16,
@@ -226,7 +232,7 @@ __device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t
     if (p.out.n_out > 1) __threadfence_system();
   } else {
     // Partial result of this split: un-normalised fp32 accumulator and row sum.
-    const size_t plane = static_cast<size_t>(gridDim.y) * p.S;  // rows per split
+    const size_t plane = static_cast<size_t>(p.BH) * p.S;  // rows per split
     float* arow = p.acc + (split * plane + grow) * kDim + half * 64;
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {
@@ -324,9 +330,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
     }
     // Never leave with a copy in flight: wait (bounded) for the last fill of every slot.
-    mbar_wait(&sm.q_full, 0, abort, p.status);
+    mbar_drain(&sm.q_full, 0, p.status);
     for (int s = 0; s < kSlots; ++s)
-      if (issued[s] > 0) mbar_wait(&sm.kv_full[s], (issued[s] - 1) & 1, abort, p.status);
+      if (issued[s] > 0) mbar_drain(&sm.kv_full[s], (issued[s] - 1) & 1, p.status);
   } else if (warp == 1) {
     // ------------------------------------------------------------ UMMA issuer (whole warp, elect.sync issues)
     auto wait = [&](uint64_t* bar, uint32_t parity) { return mbar_wait_warp(bar, parity, abort, p.status); };
@@ -392,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // Drain: every UMMA issued above has completed before TMEM is released.
     tc_commit_warp(&sm.drain);
-    wait(&sm.drain, 0);
+    mbar_drain(&sm.drain, 0, p.status);
   } else {
     // ------------------------------------------------------------ softmax + epilogue
     const int sw = warp - 2;                  // softmax warp index 0 .. 2*kSoftmaxWarps-1
@@ -433,15 +439,310 @@ __global__ void __launch_bounds__(kThreads, 1)
         row_sum_chunk(pk1, l0, l1);
       }
       // Row sum over all 128 KV columns: this warp's half plus the other half's partial.
-      sm.l_part[t][half][row] = (l0.x + l0.y) + (l1.x + l1.y);
+      sm.l_part[0][t][half][row] = (l0.x + l0.y) + (l1.x + l1.y);
       named_barrier_sync(1 + t, 32 * kSoftmaxWarps);
-      const float l = sm.l_part[t][0][row] + sm.l_part[t][1][row];
+      const float l = sm.l_part[0][t][0][row] + sm.l_part[0][t][1][row];
       if (ok) ok = mbar_wait_warp(&sm.o_full[t], 0, abort, p.status);
       if (ok) {
         tc_fence_after();
         const uint32_t o_addr = tmem + lane_off + 256 + t * 128 + half * 64;
         const size_t grow = static_cast<size_t>(row_base) + (t0 + t) * kTile + row;  // global query row
         store_rows(p, o_addr, grow, half, split, l, sm.q[t] + (sw % kSoftmaxWarps) * 4096);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Persistent form: one CTA per SM walks work items w = blockIdx.x, blockIdx.x + gridDim.x, ...,
+// an item being what one CTA of attend_kernel does (two query tiles of one (batch, head), one KV
+// split). The barriers keep counting across items, so the next item's Q and K/V loads and its
+// first S = Q K^T run while the softmax warps are still in the current item's epilogue, instead
+// of after the CTA has exited and a new one has started, allocated TMEM and loaded its tiles.
+// Ordering across items, beyond that of attend_kernel:
+//   * S_t(0) of item i+1 overwrites tile t's S/P columns after the last P.V of item i, which the
+//     issuer issued after every softmax warp of tile t had handed over its last P: safe.
+//   * P.V_t(0) of item i+1 overwrites O_t; the softmax warps of tile t hand over P_t(0) of item
+//     i+1 only after they have read O_t of item i (tcgen05.ld + wait), so the issuer's wait for
+//     that P orders the overwrite after the read.
+//   * Q of item i+1 is loaded once S(last) of item i has completed (no later UMMA reads Q).
+//   * A ring slot is refilled once the UMMAs reading its previous tile have completed, known
+//     from commits the issuer makes anyway: K_b by the commit after S_{nt-1}(b), V_b by the one
+//     after S_{nt-1}(b+1), and the item's last V by the o_full commit.
+// Used when the CTA itself writes plain (not TMA-staged) output -- the TMA-staged epilogue
+// borrows the Q buffers, which this form refills early -- and every item has the same number of
+// query tiles nt (an even tile count, or one tile): the producer follows the commits on
+// s_full[nt-1] and o_full[nt-1] one completion at a time, which it could not do for a barrier
+// whose completions it skips during items of the other size.
+struct Item {
+  int bh, t0, nt, split, kv0, n_kv;
+};
+
+__device__ __forceinline__ Item decode_item(const Params& p, int w) {
+  Item it;
+  it.split = w % p.n_splits;
+  const int rest = w / p.n_splits;
+  const int pair = rest % p.n_pairs;
+  it.bh = rest / p.n_pairs;
+  it.t0 = pair * 2;
+  it.nt = min(2, p.n_tiles - it.t0);
+  it.kv0 = static_cast<int>(static_cast<long long>(p.n_tiles) * it.split / p.n_splits);
+  it.n_kv = static_cast<int>(static_cast<long long>(p.n_tiles) * (it.split + 1) / p.n_splits) - it.kv0;
+  return it;
+}
+
+// Completion counter of one of the issuer's commit barriers, as the producer sees it. A parity
+// wait can only tell the barrier's current phase from the one before it, so completion #idx
+// (0-based) is awaited by stepping through every completion after the last one seen: a wait for
+// a phase two ahead would return at once, and one for a phase already seen is skipped.
+struct CommitTrack {
+  uint64_t* bar;
+  uint32_t seen;  // completions known to have happened
+};
+__device__ __forceinline__ bool await_completion(CommitTrack& c, uint32_t idx, volatile int* abort, int* status) {
+  for (; c.seen <= idx; ++c.seen)
+    if (!mbar_wait_warp(c.bar, c.seen & 1, abort, status)) return false;
+  return true;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attend_persistent_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                             const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Smem& sm = *smem_ptr(smem_raw);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const bool leader = lane == 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    for (int s = 0; s < kSlots; ++s) mbar_init(&sm.kv_full[s], 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(&sm.s_full[t], 1);
+      mbar_init(&sm.p_part[t][0], kSoftmaxWarps);
+      mbar_init(&sm.p_part[t][1], kSoftmaxWarps);
+      mbar_init(&sm.o_full[t], 1);
+    }
+    mbar_init(&sm.drain, 1);
+    sm.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  volatile int* abort = &sm.abort;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer (whole warp, lane 0 issues)
+    if (leader) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+    }
+    // Commit barriers and how many completions the issuer will have made on each before the
+    // current item: [0, 1] = s_full[t], [2, 3] = o_full[t].
+    CommitTrack track[4] = {{&sm.s_full[0], 0}, {&sm.s_full[1], 0}, {&sm.o_full[0], 0}, {&sm.o_full[1], 0}};
+    uint32_t made[4] = {0, 0, 0, 0};
+    // Release of the tile that last filled each ring slot: (commit barrier, completion index).
+    int rel_bar[kSlots];
+    uint32_t rel_idx[kSlots];
+    int q_rel_bar = -1;  // release of the Q tiles: the previous item's last S
+    uint32_t q_rel_idx = 0;
+    uint32_t g = 0, q_fills = 0;  // K/V loads and Q loads issued
+    bool ok = true;
+    for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x) {
+      const Item it = decode_item(p, w);
+      const int sb = it.nt - 1, ob = 2 + it.nt - 1;  // barriers that release this item's tiles
+      const uint32_t base_s = made[sb], base_o = made[ob];
+      const int row_base = it.bh * p.S;
+      // The Q tiles first: the previous item's last S is the latest completion any of this
+      // item's first loads needs, so the slot waits of K_0 and V_0 that follow return at once
+      // (and S(0) needs Q and K_0 together in any case).
+      if (q_rel_bar >= 0 && !await_completion(track[q_rel_bar], q_rel_idx, abort, p.status)) break;
+      if (leader) {
+        mbar_arrive_expect_tx(&sm.q_full, it.nt * kTileBytes);
+        for (int t = 0; t < it.nt; ++t) {
+          const int row = row_base + (it.t0 + t) * kTile;
+          tma_load_2d(sm.q[t], &tm_q, 0, row, &sm.q_full);
+          tma_load_2d(sm.q[t] + kHalfBytes, &tm_q, 64, row, &sm.q_full);
+        }
+      }
+      __syncwarp();
+      ++q_fills;
+      for (int n = 0; n < 2 * it.n_kv; ++n) {
+        const int slot = g % kSlots;
+        if (g >= kSlots && !await_completion(track[rel_bar[slot]], rel_idx[slot], abort, p.status)) {
+          ok = false;
+          break;
+        }
+        if (leader) {
+          mbar_arrive_expect_tx(&sm.kv_full[slot], kTileBytes);
+          const void* map = (n & 1) ? static_cast<const void*>(&tm_v) : static_cast<const void*>(&tm_k);
+          const int row = row_base + (it.kv0 + (n >> 1)) * kTile;
+          tma_load_2d(sm.kv[slot], map, 0, row, &sm.kv_full[slot]);
+          tma_load_2d(sm.kv[slot] + kHalfBytes, map, 64, row, &sm.kv_full[slot]);
+        }
+        __syncwarp();
+        ++g;
+        const int b = n >> 1;
+        if (!(n & 1)) {
+          rel_bar[slot] = sb;  // K_b: read by S(b)
+          rel_idx[slot] = base_s + b;
+        } else if (b < it.n_kv - 1) {
+          rel_bar[slot] = sb;  // V_b: read by P.V(b), covered by the commit after S(b+1)
+          rel_idx[slot] = base_s + b + 1;
+        } else {
+          rel_bar[slot] = ob;  // the item's last V: covered by the o_full commit
+          rel_idx[slot] = base_o;
+        }
+      }
+      q_rel_bar = sb;
+      q_rel_idx = base_s + it.n_kv - 1;
+      for (int t = 0; t < it.nt; ++t) {
+        made[t] += it.n_kv;
+        made[2 + t] += 1;
+      }
+    }
+    // Never leave with a copy in flight: wait (bounded) for the last fill of Q and of every slot.
+    if (q_fills > 0) mbar_drain(&sm.q_full, (q_fills - 1) & 1, p.status);
+    for (uint32_t s = 0; s < kSlots; ++s) {
+      const uint32_t fills = g > s ? (g - s + kSlots - 1) / kSlots : 0;
+      if (fills > 0) mbar_drain(&sm.kv_full[s], (fills - 1) & 1, p.status);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ UMMA issuer (whole warp, elect.sync issues)
+    auto wait = [&](uint64_t* bar, uint32_t parity) { return mbar_wait_warp(bar, parity, abort, p.status); };
+    const uint32_t q_lo = umma_desc_lo(smem_u32(sm.q[0]), 16);
+    const uint32_t k_lo = umma_desc_lo(smem_u32(sm.kv[0]), 16);
+    const uint32_t v_lo = umma_desc_lo(smem_u32(sm.kv[0]), kHalfBytes);
+    constexpr uint32_t kTile16 = kTileBytes >> 4;
+    auto qk = [&](int t, int slot) {
+#pragma unroll
+      for (int kc = 0; kc < 8; ++kc) {
+        const uint32_t kcoff = (kc >> 2) * (kHalfBytes >> 4) + (kc & 3) * 2;
+        umma_ss_warp_lo(tmem + t * 128, q_lo + t * kTile16 + kcoff, k_lo + slot * kTile16 + kcoff, kIdescQK,
+                        kc > 0);
+      }
+    };
+    uint32_t g0 = 0, items = 0;     // first K/V load of the item, items done
+    uint32_t blocks[2] = {0, 0};    // KV blocks done per tile: p_part phases consumed
+    auto kv_ready = [&](uint32_t n) { return wait(&sm.kv_full[n % kSlots], (n / kSlots) & 1); };
+    bool ok = true;
+    for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x) {
+      const Item it = decode_item(p, w);
+      ok = wait(&sm.q_full, items & 1) && kv_ready(g0);
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (t < it.nt) {
+          qk(t, g0 % kSlots);
+          tc_commit_warp(&sm.s_full[t]);
+        }
+      }
+      for (int j = 0; ok && j < it.n_kv; ++j) {
+        const uint32_t nv = g0 + 2 * j + 1, nk = g0 + 2 * j + 2;
+        const bool last = (j == it.n_kv - 1);
+        ok = kv_ready(nv) && (last || kv_ready(nk));
+        if (!ok) break;
+        const uint32_t vslot = v_lo + (nv % kSlots) * kTile16;
+        const int kslot = nk % kSlots;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (t >= it.nt) break;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            ok = wait(&sm.p_part[t][c], (blocks[t] + j) & 1);
+            if (!ok) break;
+            tc_fence_after();
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int kc = (i & 1) + 2 * c + 4 * (i >> 1);
+              umma_ts_warp_lo(tmem + 256 + t * 128, tmem + t * 128 + p_col(kc), vslot + kc * (2048 >> 4), kIdescPV,
+                              (j > 0 || c > 0 || i > 0) ? 1u : 0u);
+            }
+          }
+          if (!ok) break;
+          if (last) {
+            tc_commit_warp(&sm.o_full[t]);
+            continue;
+          }
+          qk(t, kslot);
+          tc_commit_warp(&sm.s_full[t]);
+        }
+      }
+      for (int t = 0; t < it.nt; ++t) blocks[t] += it.n_kv;
+      g0 += 2 * it.n_kv;
+      ++items;
+    }
+    tc_commit_warp(&sm.drain);
+    mbar_drain(&sm.drain, 0, p.status);
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int sw = warp - 2;
+    const int t = sw / kSoftmaxWarps;
+    const int half = (sw % kSoftmaxWarps) / 4;
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t s_addr = tmem + lane_off + t * 128 + half * 64;
+    const uint32_t o_addr = tmem + lane_off + 256 + t * 128 + half * 64;
+    uint32_t s_seen = 0, o_seen = 0, items = 0;  // s_full[t] / o_full[t] completions consumed, items of tile t
+    // Once a wait has failed the warp does no more work, but it still meets its tile's named
+    // barrier once per item, as its partner warps (which may not have seen the failure yet) do.
+    bool ok = true;
+    for (int w = blockIdx.x; w < p.n_items; w += gridDim.x) {
+      const Item it = decode_item(p, w);
+      if (t >= it.nt) continue;
+      float2 l0 = make_float2(0.f, 0.f), l1 = make_float2(0.f, 0.f);
+      for (int j = 0; ok && j < it.n_kv; ++j, ++s_seen) {
+        ok = mbar_wait_warp(&sm.s_full[t], s_seen & 1, abort, p.status);
+        if (!ok) break;
+        tc_fence_after();
+        uint32_t ra[32], rb[32], pk0[16], pk1[16];
+        tmem_ld_32x32b_x32(s_addr, ra);
+        tmem_wait_ld(ra);
+        tmem_ld_32x32b_x32(s_addr + 32, rb);
+        exp_chunk(ra, pk0);
+        tmem_st_32x32b_x16(s_addr, pk0);
+        tmem_wait_ld(rb);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_part[t][0]);
+        exp_chunk(rb, pk1);
+        tmem_st_32x32b_x16(s_addr + 16, pk1);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sm.p_part[t][1]);
+        row_sum_chunk(pk0, l0, l1);
+        row_sum_chunk(pk1, l0, l1);
+      }
+      const int lb = items & 1;
+      sm.l_part[lb][t][half][row] = (l0.x + l0.y) + (l1.x + l1.y);
+      named_barrier_sync(1 + t, 32 * kSoftmaxWarps);
+      const float l = sm.l_part[lb][t][0][row] + sm.l_part[lb][t][1][row];
+      if (ok) ok = mbar_wait_warp(&sm.o_full[t], o_seen & 1, abort, p.status);
+      ++o_seen;
+      ++items;
+      if (ok) {
+        tc_fence_after();
+        const size_t grow = static_cast<size_t>(it.bh) * p.S + (it.t0 + t) * kTile + row;
+        store_rows(p, o_addr, grow, half, it.split, l, nullptr);
       }
     }
   }
@@ -551,10 +852,15 @@ int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return FLK_ERR_CUDA;
   static bool configured[64] = {};
+  static int sm_count[64] = {};
   if (dev < 0 || dev >= 64) return FLK_ERR_UNSUPPORTED;
   if (!configured[dev]) {
     if (cudaFuncSetAttribute(attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(attend_smem_bytes())) != cudaSuccess)
+                             static_cast<int>(attend_smem_bytes())) != cudaSuccess ||
+        cudaFuncSetAttribute(attend_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(attend_smem_bytes())) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        sm_count[dev] <= 0)
       return FLK_ERR_CUDA;
     configured[dev] = true;
   }
@@ -566,6 +872,11 @@ int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
   p.S = S;
   p.n_tiles = S / kTile;
   p.n_splits = splits;
+  p.BH = B * H;
+  p.n_pairs = (p.n_tiles + 1) / 2;
+  const long long items = static_cast<long long>(p.BH) * p.n_pairs * splits;
+  if (items > INT32_MAX) return FLK_ERR_UNSUPPORTED;
+  p.n_items = static_cast<int>(items);
   p.out = out;
   p.tma_out = (out.merged && out.n_out > 1 && splits == 1) ? 1 : 0;
   if (p.tma_out)
@@ -575,9 +886,13 @@ int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
   p.acc = splits > 1 ? static_cast<float*>(workspace) : nullptr;
   p.lsum = splits > 1 ? p.acc + static_cast<size_t>(splits) * rows * kDim : nullptr;
   p.status = status;
-  const dim3 grid((p.n_tiles + 1) / 2, B * H, splits);
+  // The persistent form whenever the CTAs write plain output and every item has the same number
+  // of query tiles (its producer tracks one commit barrier per tile count); the one-item-per-CTA
+  // form for the TMA-staged epilogue, which borrows the Q buffers, and for odd tile counts.
+  const bool persistent = !p.tma_out && (p.n_tiles % 2 == 0 || p.n_tiles == 1);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
+  cfg.gridDim = persistent ? dim3(static_cast<unsigned>(std::min<long long>(items, sm_count[dev])))
+                           : dim3(p.n_pairs, p.BH, splits);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = attend_smem_bytes();
   cfg.stream = stream;
@@ -586,7 +901,9 @@ int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, attend_kernel, mq, mk, mv, p) != cudaSuccess) return FLK_ERR_CUDA;
+  if (cudaLaunchKernelEx(&cfg, persistent ? attend_persistent_kernel : attend_kernel, mq, mk, mv, p) !=
+      cudaSuccess)
+    return FLK_ERR_CUDA;
   if (cudaGetLastError() != cudaSuccess) return FLK_ERR_CUDA;
   if (splits > 1) {
     const long long threads = rows * (kDim / 8);

@@ -381,7 +381,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     // only after its MMAs (the consumers of those copies) have drained.
     if (rank == 0)
       for (int s = 0; s < kPairStages; ++s)
-        if (issued[s] > 0) mbar_wait_warp(&sm.full[s], (issued[s] - 1) & 1, abort, p.status);
+        if (issued[s] > 0) mbar_drain(&sm.full[s], (issued[s] - 1) & 1, p.status);
   } else if (warp == 1) {
     if (rank == 0) {
       // ---------------------------------------------------------------- UMMA issuer (even CTA)
@@ -407,7 +407,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         if (ok) tc_commit_pair_both_warp(&sm.acc_full[buf]);
       }
       tc_commit_pair_own_warp(&sm.drain);
-      mbar_wait_warp(&sm.drain, 0, abort, p.status);
+      mbar_drain(&sm.drain, 0, p.status);
     }
   } else {
     // -------------------------------------------------------------------- epilogue (both CTAs)

@@ -105,6 +105,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   return mbar_wait_slow(bar, parity, abort, status);
 }
 
+// Wait for a phase that completes on its own -- TMA copies or UMMAs this CTA has already
+// issued -- before the CTA frees the memory they write (tensor memory) or exits (shared
+// memory). Unlike mbar_wait it does not give up when the CTA is aborting, since that is exactly
+// when in-flight work must still be waited for; it is bounded by the same time limit.
+static __device__ __noinline__ bool mbar_drain(uint64_t* bar, uint32_t parity, int* status) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t spin = 1; spin < kWaitSpinCap; ++spin) {
+    if (mbar_test_sleep(bar, parity)) return true;
+    if (spin % kPollsPerCheck == 0 && globaltimer_ns() - t0 > kWaitLimitNs) break;
+  }
+  atomicExch(status, kErrDeviceTimeout);
+  return false;
+}
+
 // mbar_wait for all 32 lanes of a converged warp, with a warp-uniform outcome: one vote on a
 // single try_wait decides the common case without divergent code; the lanes go to the slow
 // path together only when the phase is still open.

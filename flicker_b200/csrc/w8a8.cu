@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       }
       for (int s = 0; s < kStages; ++s)
-        if (issued[s] > 0) mbar_wait(&sm.full[s], (issued[s] - 1) & 1, abort, p.status);
+        if (issued[s] > 0) mbar_drain(&sm.full[s], (issued[s] - 1) & 1, p.status);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (ok) tc_commit(&sm.acc_full[buf]);
       }
       tc_commit(&sm.drain);
-      mbar_wait(&sm.drain, 0, abort, p.status);
+      mbar_drain(&sm.drain, 0, p.status);
     }
   } else {
     // -------------------------------------------------------------------- epilogue
