@@ -60,3 +60,23 @@ def test_shards_gathered_into_every_buffer(b, h, s, shards):
     full = fb.attend_merged(q, k, v).float()
     err = (outs[0].float() - full).abs().max().item()
     assert err <= 2e-2
+
+
+# Even tile counts run the persistent kernel for attend_merged, while a gathering call into two
+# local buffers runs the one-item-per-CTA kernel with its TMA-staged epilogue: (1, 24, 4608) is
+# 432 items on 148 CTAs, (2, 24, 1536) 288 items, (3, 2, 128) single-tile items.
+@pytest.mark.parametrize("b,h,s", [(1, 24, 4608), (2, 24, 1536), (3, 2, 128), (1, 16, 2048)])
+def test_attend_persistent_matches(b, h, s):
+    """The persistent kernel (items walked by one CTA per SM, barriers counting across items)
+    computes exactly what one CTA per item computes: bit-identical outputs."""
+    q, k, v = random_qkv(b, h, s, b * 100 + h + s)
+    lib = _lib.lib()
+    # both forms only where the call is not split over KV
+    assert lib.flk_attend_workspace_size(b, h, s, 128) == 0
+    persistent = fb.attend_merged(q, k, v)
+    outs = [torch.full((b, s, h * 128), float("nan"), dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    gather_call(q, k, v, outs, h, 0)
+    torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(o, persistent)
+    assert lib.flk_device_status() == 0

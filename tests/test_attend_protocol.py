@@ -1,0 +1,282 @@
+"""A randomised model of the barrier protocol of ``attend_persistent_kernel`` (csrc/attend.cu).
+
+The kernel's three roles are restated as Python generators that yield their waits, in the same
+order and with the same completion indices as the CUDA code:
+
+* the producer (TMA warp): per item the Q tiles, then K_0, V_0, K_1, ... into a 4-slot ring,
+  each slot refilled once the commit that covers its previous tile's readers has completed,
+  awaited one completion at a time (``await_completion``);
+* the issuer (UMMA warp): S_t(0), then per KV block P.V_t(j) in two chunks and S_t(j+1), with
+  commits on s_full[t] and, after an item's last block, o_full[t];
+* 16 softmax warps: exp of S into P (two hand-over chunks), the row-sum exchange over a named
+  barrier (double-buffered by item parity) and the epilogue read of O.
+
+The 'hardware' runs at random times: TMA copies land, UMMAs execute in issue order, commits
+arrive. mbarrier waits use the hardware's parity semantics (a wait for parity p returns once the
+current phase's parity differs from p), and every wait checks that this answer is the intended
+one, i.e. that the awaited completion has happened and the barrier is not a further phase on.
+Every operand read (Q, K and V slots by UMMAs, S and O by the softmax warps, P by P.V, the
+partner's row sum) checks the version it must see. Warps react within nanoseconds while copies
+and UMMAs take microseconds, so a ready warp mostly runs first.
+"""
+from __future__ import annotations
+
+import random
+
+import pytest
+
+
+class ProtocolError(AssertionError):
+    pass
+
+
+class Bar:
+    def __init__(self, name: str, count: int = 1):
+        self.name, self.count, self.arrived, self.completed = name, count, 0, 0
+
+    def arrive(self):
+        self.arrived += 1
+        if self.arrived == self.count:
+            self.arrived = 0
+            self.completed += 1
+
+
+def decode(w, n_tiles, n_splits):
+    """decode_item (attend.cu): work item -> (query tiles, KV range)."""
+    n_pairs = (n_tiles + 1) // 2
+    split = w % n_splits
+    pair = (w // n_splits) % n_pairs
+    t0 = pair * 2
+    kv0 = n_tiles * split // n_splits
+    return dict(w=w, nt=min(2, n_tiles - t0), n_kv=n_tiles * (split + 1) // n_splits - kv0)
+
+
+def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, step_completions=True):
+    n_items = bh * ((n_tiles + 1) // 2) * n_splits
+    items = [decode(w, n_tiles, n_splits) for w in range(cta, n_items, grid)]
+    q_full = Bar("q_full")
+    kv_full = [Bar(f"kv_full{s}") for s in range(4)]
+    s_full = [Bar(f"s_full{t}") for t in range(2)]
+    p_part = [[Bar(f"p_part{t}{c}", 8) for c in range(2)] for t in range(2)]
+    o_full = [Bar(f"o_full{t}") for t in range(2)]
+    qbuf, q_inflight = [None, None], [False, False]
+    kv, kv_inflight = [None] * 4, [False] * 4
+    s_reg = [[[None] * 2 for _ in range(4)] for _ in range(2)]  # [tile][quad][half]
+    p_reg = [[[[None, None] for _ in range(2)] for _ in range(4)] for _ in range(2)]  # [tile][quad][half][chunk]
+    o_reg = [None, None]
+    l_part = [[[[None] * 4 for _ in range(2)] for _ in range(2)] for _ in range(2)]  # [parity][tile][half][quad]
+    tma, mma = [], []
+    named = [[0, 0], [0, 0]]  # per tile: arrivals, generation
+
+    def answer(b, k):
+        done = (b.completed & 1) != (k & 1)
+        if done and b.completed != k + 1:
+            raise ProtocolError(f"wait for {b.name} #{k} returned with {b.completed} completions")
+        if not done and b.completed >= k + 2:
+            raise ProtocolError(f"wait for {b.name} #{k} missed: {b.completed} completions")
+        return done
+
+    def producer():
+        bars = [s_full[0], s_full[1], o_full[0], o_full[1]]
+        seen, made = [0] * 4, [0] * 4
+        rel, q_rel, g = [None] * 4, None, 0
+
+        def await_completion(bid, idx):
+            if step_completions:
+                while seen[bid] <= idx:
+                    yield ("wait", bars[bid], seen[bid])
+                    seen[bid] += 1
+            elif idx >= seen[bid]:  # planted mistake: jump straight to the wanted completion
+                yield ("wait", bars[bid], idx)
+                seen[bid] = idx + 1
+
+        for it in items:
+            sb, ob = it["nt"] - 1, 2 + it["nt"] - 1
+            base_s, base_o = made[sb], made[ob]
+            if q_rel is not None:
+                yield from await_completion(*q_rel)
+            for t in range(it["nt"]):
+                q_inflight[t] = True
+            tma.append(("q", it["w"], it["nt"]))
+            for n in range(2 * it["n_kv"]):
+                slot = g % 4
+                if g >= 4:
+                    yield from await_completion(*rel[slot])
+                if kv_inflight[slot]:
+                    raise ProtocolError("slot refilled while a copy into it is in flight")
+                kv_inflight[slot] = True
+                tma.append(("kv", slot, ("V" if n & 1 else "K", it["w"], n >> 1)))
+                g += 1
+                b = n >> 1
+                if not n & 1:
+                    rel[slot] = (sb, base_s + b)
+                elif b < it["n_kv"] - 1:
+                    rel[slot] = (sb, base_s + b + 1)
+                else:
+                    rel[slot] = (ob, base_o)
+            q_rel = (sb, base_s + it["n_kv"] - 1)
+            for t in range(it["nt"]):
+                made[t] += it["n_kv"]
+                made[2 + t] += 1
+
+    def issuer():
+        g0, done, blocks = 0, 0, [0, 0]
+        for it in items:
+            yield ("wait", q_full, done)
+            yield ("wait", kv_full[g0 % 4], g0 // 4)
+            for t in range(it["nt"]):
+                mma.append(("S", it["w"], t, 0, g0 % 4))
+                mma.append(("commit", s_full[t]))
+            n_kv = it["n_kv"]
+            for j in range(n_kv):
+                nv, nk = g0 + 2 * j + 1, g0 + 2 * j + 2
+                last = j == n_kv - 1
+                yield ("wait", kv_full[nv % 4], nv // 4)
+                if not last:
+                    yield ("wait", kv_full[nk % 4], nk // 4)
+                for t in range(it["nt"]):
+                    for c in range(2):
+                        yield ("wait", p_part[t][c], blocks[t] + j)
+                        mma.append(("PV", it["w"], t, j, c, nv % 4))
+                    if last:
+                        mma.append(("commit", o_full[t]))
+                    else:
+                        mma.append(("S", it["w"], t, j + 1, nk % 4))
+                        mma.append(("commit", s_full[t]))
+            for t in range(it["nt"]):
+                blocks[t] += n_kv
+            g0 += 2 * n_kv
+            done += 1
+
+    def softmax(t, quad, half):
+        s_seen = o_seen = n_done = 0
+        for it in items:
+            if t >= it["nt"]:
+                continue
+            n_kv = it["n_kv"]
+            for j in range(n_kv):
+                yield ("wait", s_full[t], s_seen)
+                s_seen += 1
+                if s_reg[t][quad][half] != ("S", it["w"], t, j):
+                    raise ProtocolError(f"softmax read S {s_reg[t][quad][half]}, wanted {('S', it['w'], t, j)}")
+                for c in range(2):
+                    yield ("step",)
+                    p_reg[t][quad][half][c] = ("P", it["w"], t, j)
+                    p_part[t][c].arrive()
+            lb = n_done & 1
+            l_part[lb][t][half][quad] = it["w"]
+            gen = named[t][1]
+            named[t][0] += 1
+            if named[t][0] == 8:
+                named[t] = [0, gen + 1]
+            yield ("named", t, gen)
+            if l_part[lb][t][1 - half][quad] != it["w"]:
+                raise ProtocolError("partner's row sum overwritten before it was read")
+            yield ("wait", o_full[t], o_seen)
+            o_seen += 1
+            n_done += 1
+            yield ("step",)
+            if o_reg[t] != (it["w"], 2 * n_kv - 1):
+                raise ProtocolError(f"epilogue read O {o_reg[t]}, wanted {(it['w'], 2 * n_kv - 1)}")
+
+    def execute_mma():
+        e = mma.pop(0)
+        if e[0] == "commit":
+            e[1].arrive()
+        elif e[0] == "S":
+            _, w, t, j, slot = e
+            if qbuf[t] != w or q_inflight[t]:
+                raise ProtocolError(f"S read Q {qbuf[t]} (copy in flight: {q_inflight[t]}), wanted {w}")
+            if kv[slot] != ("K", w, j) or kv_inflight[slot]:
+                raise ProtocolError(f"S read K {kv[slot]}, wanted {('K', w, j)}")
+            for quad in range(4):
+                for half in range(2):
+                    s_reg[t][quad][half] = ("S", w, t, j)
+                    p_reg[t][quad][half] = [None, None]
+        else:
+            _, w, t, j, c, slot = e
+            if kv[slot] != ("V", w, j) or kv_inflight[slot]:
+                raise ProtocolError(f"P.V read V {kv[slot]}, wanted {('V', w, j)}")
+            for quad in range(4):
+                for half in range(2):
+                    if p_reg[t][quad][half][c] != ("P", w, t, j):
+                        raise ProtocolError(f"P.V read P {p_reg[t][quad][half][c]}, wanted {('P', w, t, j)}")
+            step = 2 * j + c
+            if step > 0 and o_reg[t] != (w, step - 1):
+                raise ProtocolError(f"P.V accumulated onto O {o_reg[t]}, wanted {(w, step - 1)}")
+            o_reg[t] = (w, step)
+
+    def land_copy(k):
+        e = tma.pop(k)
+        if e[0] == "q":
+            for t in range(e[2]):
+                qbuf[t], q_inflight[t] = e[1], False
+            q_full.arrive()
+        else:
+            kv[e[1]], kv_inflight[e[1]] = e[2], False
+            kv_full[e[1]].arrive()
+
+    agents = [producer(), issuer()] + [softmax(t, q, h) for t in range(2) for q in range(4) for h in range(2)]
+    req = [None] * len(agents)
+
+    def advance(i):
+        req[i] = next(agents[i], None)
+
+    for i in range(len(agents)):
+        advance(i)
+
+    def ready(i):
+        r = req[i]
+        if r is None:
+            return False
+        if r[0] == "step":
+            return True
+        if r[0] == "wait":
+            return answer(r[1], r[2])
+        return named[r[1]][1] > r[2]
+
+    for _ in range(1_000_000):
+        warps = [i for i in range(len(agents)) if ready(i)]
+        if warps and rng.random() > p_hw:
+            advance(rng.choice(warps))
+            continue
+        hw = [("copy", k) for k in range(len(tma))] + ([("mma", 0)] if mma else [])
+        acts = [("warp", i) for i in warps] + hw
+        if not acts:
+            if all(r is None for r in req):
+                assert not tma and not mma
+                return len(items)
+            raise ProtocolError("deadlock: " + ", ".join(f"{i}: {r}" for i, r in enumerate(req) if r is not None))
+        kind, i = rng.choice(acts)
+        if kind == "warp":
+            advance(i)
+        elif kind == "copy":
+            land_copy(i)
+        else:
+            execute_mma()
+    raise ProtocolError("no progress")
+
+
+# (tile count, KV splits, batch x heads, grid): the persistent kernel runs even tile counts and
+# single tiles, with and without KV splits, one or several items per CTA, single-block items.
+CASES = [(2, 1, 2, 1), (4, 1, 3, 2), (6, 4, 1, 1), (8, 3, 3, 2), (2, 2, 3, 1), (1, 1, 5, 2), (4, 4, 3, 2),
+         (6, 6, 2, 3), (10, 1, 2, 1)]
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_protocol_holds(case):
+    n_tiles, n_splits, bh, grid = case
+    rng = random.Random(hash(case) & 0xFFFF)
+    for cta in range(grid):
+        for _ in range(6):
+            for p_hw in (0.02, 0.3):
+                assert run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw) > 0
+
+
+def test_model_catches_a_skipped_completion():
+    """Planted in the model: a producer that waits for the completion it needs without stepping
+    through the ones before it (a parity wait two phases ahead returns at once)."""
+    rng = random.Random(7)
+    with pytest.raises(ProtocolError):
+        for _ in range(50):
+            run_cta(2, 1, 3, 1, 0, rng, 0.3, step_completions=False)
