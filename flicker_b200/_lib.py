@@ -51,6 +51,8 @@ SIGNATURES = {
                                ctypes.POINTER(ctypes.c_float)]),
     "flk_device_status": (_int, []),
     "flk_selftest_wait_timeout": (_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "flk_selftest_quotient": (_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p,
+                                     ctypes.c_void_p, ctypes.c_void_p]),
     "flk_error_string": (ctypes.c_char_p, [_int]),
     "flk_abi_version": (_int, []),
 }

@@ -35,6 +35,7 @@
 
 #include "flicker_b200.h"
 #include "ptx.cuh"
+#include "quotient.cuh"
 
 namespace flk {
 
@@ -177,11 +178,13 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int c0, int
 }
 
 // Epilogue of one softmax warp: its 32 rows x 64 columns of O from TMEM, either normalised and
-// rounded to bf16 (o = bf16(acc / l), kernels.py:130) or, for a KV split, the fp32 partials.
+// rounded to bf16 (o = bf16(acc / l), kernels.py:130, the quotient correctly rounded through one
+// reciprocal per row) or, for a KV split, the fp32 partials.
 // Kept out of line so that this once-per-CTA code sits apart from the KV loop's code. `stage`
 // is this warp's 4 KB of shared memory (1024-byte aligned, free once the tile's MMAs are done).
 __device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t grow, int half, int split, float l,
                                         uint8_t* stage) {
+  const float rl = __frcp_rn(l);
   if (p.n_splits == 1 && p.tma_out) {
     // Stage the 32 x 64 block in the 128-byte-swizzled layout the maps expect (16-byte unit j of
     // row r at position j ^ (r & 7): conflict-free), then one lane stores it to every buffer.
@@ -194,7 +197,8 @@ __device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t
       uint32_t pk[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i)
-        pk[i] = pack_bf16x2(__fdiv_rn(__uint_as_float(r[2 * i]), l), __fdiv_rn(__uint_as_float(r[2 * i + 1]), l));
+        pk[i] = pack_bf16x2(quotient_rn(__uint_as_float(r[2 * i]), l, rl),
+                            quotient_rn(__uint_as_float(r[2 * i + 1]), l, rl));
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int j = c * 4 + i;
@@ -226,7 +230,8 @@ __device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t
       uint32_t pk[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i)
-        pk[i] = pack_bf16x2(__fdiv_rn(__uint_as_float(r[2 * i]), l), __fdiv_rn(__uint_as_float(r[2 * i + 1]), l));
+        pk[i] = pack_bf16x2(quotient_rn(__uint_as_float(r[2 * i]), l, rl),
+                            quotient_rn(__uint_as_float(r[2 * i + 1]), l, rl));
       store_out(p.out, orow + c * 32, pk);
     }
     if (p.out.n_out > 1) __threadfence_system();
@@ -773,8 +778,9 @@ __global__ void __launch_bounds__(256) combine_splits_kernel(const float* __rest
     l += lsum[s * rows + row];
   }
   uint32_t pk[4];
+  const float rl = __frcp_rn(l);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) pk[i] = pack_bf16x2(__fdiv_rn(a[2 * i], l), __fdiv_rn(a[2 * i + 1], l));
+  for (int i = 0; i < 4; ++i) pk[i] = pack_bf16x2(quotient_rn(a[2 * i], l, rl), quotient_rn(a[2 * i + 1], l, rl));
   const size_t off = out_row(row, S, L) * kDim + col;
 #pragma unroll 1
   for (int d = 0; d < L.n_out; ++d) *reinterpret_cast<uint4*>(L.o[d] + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);

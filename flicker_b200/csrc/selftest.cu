@@ -1,3 +1,5 @@
+// Self-tests of device-side building blocks, each run by a GPU test.
+//
 // flk_selftest_wait_timeout: exercises the failure path of the bounded in-kernel waits.
 //
 // One warp waits on an mbarrier that nothing ever arrives at, through the same mbar_wait_warp
@@ -11,6 +13,7 @@
 
 #include "flicker_b200.h"
 #include "ptx.cuh"
+#include "quotient.cuh"
 
 namespace flk {
 int* current_device_status(int* err);
@@ -30,6 +33,17 @@ __global__ void __launch_bounds__(32) wait_timeout_kernel(int* status, int* resu
   if (threadIdx.x == 0) *result = ok ? 1 : 0;
 }
 
+// q_fast[i] = a[i] / b[i] through quotient_rn (one reciprocal per divisor, as the attend
+// epilogue uses it per row); q_ref[i] = __fdiv_rn(a[i], b[i]).
+__global__ void __launch_bounds__(256) quotient_kernel(const float* a, const float* b, long long n, float* q_fast,
+                                                       float* q_ref) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float x = a[i], y = b[i];
+  q_fast[i] = quotient_rn(x, y, __frcp_rn(y));
+  q_ref[i] = __fdiv_rn(x, y);
+}
+
 }  // namespace
 }  // namespace flk
 
@@ -39,5 +53,17 @@ extern "C" int flk_selftest_wait_timeout(int* result, void* stream) {
   int* status = flk::current_device_status(&err);
   if (status == nullptr) return err;
   flk::wait_timeout_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(status, result);
+  return cudaGetLastError() == cudaSuccess ? FLK_OK : FLK_ERR_CUDA;
+}
+
+// flk_selftest_quotient: the epilogue's reciprocal-and-correction quotient next to __fdiv_rn
+// for n operand pairs (device pointers), so a test can compare them bit for bit.
+extern "C" int flk_selftest_quotient(const float* a, const float* b, long long n, float* q_fast, float* q_ref,
+                                     void* stream) {
+  if (n < 0 || (n > 0 && (a == nullptr || b == nullptr || q_fast == nullptr || q_ref == nullptr)))
+    return FLK_ERR_INVALID_ARGUMENT;
+  if (n == 0) return FLK_OK;
+  flk::quotient_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      a, b, n, q_fast, q_ref);
   return cudaGetLastError() == cudaSuccess ? FLK_OK : FLK_ERR_CUDA;
 }

@@ -179,6 +179,11 @@ int flk_i8_gemm_s32(const int8_t* a, const int8_t* b, int M, int N, int K, int32
  */
 int flk_selftest_wait_timeout(int* result, void* stream);
 
+/* Self-test of the attend epilogue's quotient (one correctly rounded reciprocal per row, then
+ * Markstein's FMA correction per element): writes that quotient and __fdiv_rn's for n pairs of
+ * device floats (a[i] / b[i]) into q_fast and q_ref. No reference counterpart (device check). */
+int flk_selftest_quotient(const float* a, const float* b, long long n, float* q_fast, float* q_ref, void* stream);
+
 /* Reads (and clears) the device-side status word of the current device: 0 or FLK_ERR_DEVICE_TIMEOUT.
  * Synchronises the device. */
 int flk_device_status(void);
