@@ -59,6 +59,11 @@ struct alignas(1024) Smem {
   uint8_t kv[kSlots][kTileBytes];
   uint64_t q_full;
   uint64_t kv_full[kSlots];
+  // Buffer releases, one arrival (one completion) per fill, so a fill waits for the completion
+  // of the fill before it: made by the first softmax warp of the item's last query tile as soon
+  // as it has seen the commit that covers the buffer's last reader (see release_after_s).
+  uint64_t kv_empty[kSlots];
+  uint64_t q_empty;  // persistent form: the Q tiles of an item, after its last S
   uint64_t s_full[2];
   uint64_t p_part[2][2];  // [tile][column chunk]: P chunk c of every softmax warp of the tile is in TMEM
   uint64_t o_full[2];
@@ -145,6 +150,23 @@ __device__ __forceinline__ void row_sum_chunk(const uint32_t (&pk)[16], float2& 
 // the softmax warp of column half h writes the P of S columns [64h, 64h+64) packed into
 // columns [64h, 64h+32), i.e. over S columns it has already read.
 __device__ __forceinline__ uint32_t p_col(int kc) { return static_cast<uint32_t>((kc >> 2) * 64 + (kc & 3) * 8); }
+
+// Buffer releases inside an item, made by lane 0 of the first softmax warp of the item's last
+// query tile (nt-1) right after it has seen the commit on s_full[nt-1] that follows S_{nt-1}(j).
+// A commit tracks every UMMA issued before it and the issuer runs tile 0's UMMAs of a block
+// before tile 1's, so that commit covers every tile's S(j) -- K_j (ring fill g0 + 2j) is free,
+// and when j is the item's last block, so are the Q tiles -- and every tile's P.V(j-1), issued
+// before S(j): V_{j-1} (fill g0 + 2j - 1). g0 is the ring index of the item's first K/V load.
+// The item's first K and last V are released by the issuer's own commits (kv_empty right after
+// S_{nt-1}(0) and after P.V_{nt-1}(last)): at those two points the softmax warps are busy with
+// the previous item's epilogue or their row sums, and a late release would hold up the refills.
+__device__ __forceinline__ void release_after_s(Smem& sm, uint32_t g0, int j, int n_kv) {
+  if (j > 0) {
+    mbar_arrive(&sm.kv_empty[(g0 + 2 * j) % kSlots]);
+    mbar_arrive(&sm.kv_empty[(g0 + 2 * j - 1) % kSlots]);
+  }
+  if (j == n_kv - 1) mbar_arrive(&sm.q_empty);
+}
 
 // 128-column output row that holds query row `grow` (= (b * H + h) * S + s): itself in the
 // head-major layout; (b * S + s) * H_out + h0 + h when heads are merged (modules.merge_heads,
@@ -272,7 +294,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
-    for (int s = 0; s < kSlots; ++s) mbar_init(&sm.kv_full[s], 1);
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&sm.kv_full[s], 1);
+      mbar_init(&sm.kv_empty[s], 1);
+    }
+    mbar_init(&sm.q_empty, 1);
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sm.s_full[t], 1);
       mbar_init(&sm.p_part[t][0], kSoftmaxWarps);  // one arrival per softmax warp
@@ -310,20 +336,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(sm.q[t] + kHalfBytes, &tm_q, 64, row, &sm.q_full);
       }
     }
-    // Slot reuse needs no barrier of its own: the issuer commits s_full[nt-1] after the last UMMA
-    // of every block, and a commit tracks all earlier UMMAs, so its completion #(b+1) means block
-    // b's P.V (V_b) and the S for block b+1 (K_{b+1}) have run; completion #0 covers S(0) (K_0).
-    // Load n refills the slot of load n-4: K_i (n-4 = 2i) is free after completion #i,
-    // V_i (n-4 = 2i+1) after completion #(i+1).
-    uint64_t* slot_free = &sm.s_full[nt - 1];
+    // Fill f of a ring slot waits for completion #(f-1) of the slot's kv_empty. That barrier
+    // cannot complete again before this fill has landed and been read, so the parity wait always
+    // refers to its current or its previous phase, however late this warp runs.
     int issued[kSlots] = {};
     for (int n = 0; n < 2 * n_kv; ++n) {
-      const int slot = n % kSlots;
-      if (n >= kSlots) {
-        const int m = n - kSlots;
-        const int done = (m & 1) ? (m >> 1) + 1 : (m >> 1);  // completion index of slot_free to await
-        if (!mbar_wait_warp(slot_free, done & 1, abort, p.status)) break;
-      }
+      const int slot = n % kSlots, fill = n / kSlots;
+      if (fill > 0 && !mbar_wait_warp(&sm.kv_empty[slot], (fill - 1) & 1, abort, p.status)) break;
       if (leader) {
         mbar_arrive_expect_tx(&sm.kv_full[slot], kTileBytes);
         const void* map = (n & 1) ? static_cast<const void*>(&tm_v) : static_cast<const void*>(&tm_k);
@@ -366,6 +385,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_commit_warp(&sm.s_full[t]);
         }
       }
+      tc_commit_warp(&sm.kv_empty[0]);  // K_0 has been read by every tile's S(0)
     }
     for (int j = 0; ok && j < n_kv; ++j) {
       const int nv = 2 * j + 1, nk = 2 * j + 2;
@@ -393,6 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         if (last) {
+          if (t == nt - 1) tc_commit_warp(&sm.kv_empty[nv % kSlots]);  // the last V, read by every tile
           tc_commit_warp(&sm.o_full[t]);
           continue;
         }
@@ -414,12 +435,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (t < nt) {
       const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
       const uint32_t s_addr = tmem + lane_off + t * 128 + half * 64;
+      const bool releaser = t == nt - 1 && sw % kSoftmaxWarps == 0 && lane == 0;
       float2 l0 = make_float2(0.f, 0.f), l1 = make_float2(0.f, 0.f);
       bool ok = true;
       for (int j = 0; j < n_kv; ++j) {
         // Warp-uniform outcome: the tcgen05.ld/st below are .sync.aligned.
         ok = mbar_wait_warp(&sm.s_full[t], j & 1, abort, p.status);
         if (!ok) break;
+        if (releaser) release_after_s(sm, 0, j, n_kv);
         tc_fence_after();
         // Two 32-column chunks of this row's half of S; chunk 1 is loading while chunk 0 is
         // exponentiated, and each chunk's P is handed to the issuer as soon as it is in TMEM.
@@ -477,15 +500,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   * P.V_t(0) of item i+1 overwrites O_t; the softmax warps of tile t hand over P_t(0) of item
 //     i+1 only after they have read O_t of item i (tcgen05.ld + wait), so the issuer's wait for
 //     that P orders the overwrite after the read.
-//   * Q of item i+1 is loaded once S(last) of item i has completed (no later UMMA reads Q).
-//   * A ring slot is refilled once the UMMAs reading its previous tile have completed, known
-//     from commits the issuer makes anyway: K_b by the commit after S_{nt-1}(b), V_b by the one
-//     after S_{nt-1}(b+1), and the item's last V by the o_full commit.
-// Used when the CTA itself writes plain (not TMA-staged) output -- the TMA-staged epilogue
-// borrows the Q buffers, which this form refills early -- and every item has the same number of
-// query tiles nt (an even tile count, or one tile): the producer follows the commits on
-// s_full[nt-1] and o_full[nt-1] one completion at a time, which it could not do for a barrier
-// whose completions it skips during items of the other size.
+//   * Q of item i+1 is loaded once S(last) of item i has completed (q_empty, committed right
+//     after that S; no later UMMA of item i reads Q), ring slots as in attend_kernel (kv_empty).
+// Used when the CTA itself writes plain (not TMA-staged) output: the TMA-staged epilogue borrows
+// the Q buffers, which this form refills early.
 struct Item {
   int bh, t0, nt, split, kv0, n_kv;
 };
@@ -503,20 +521,6 @@ __device__ __forceinline__ Item decode_item(const Params& p, int w) {
   return it;
 }
 
-// Completion counter of one of the issuer's commit barriers, as the producer sees it. A parity
-// wait can only tell the barrier's current phase from the one before it, so completion #idx
-// (0-based) is awaited by stepping through every completion after the last one seen: a wait for
-// a phase two ahead would return at once, and one for a phase already seen is skipped.
-struct CommitTrack {
-  uint64_t* bar;
-  uint32_t seen;  // completions known to have happened
-};
-__device__ __forceinline__ bool await_completion(CommitTrack& c, uint32_t idx, volatile int* abort, int* status) {
-  for (; c.seen <= idx; ++c.seen)
-    if (!mbar_wait_warp(c.bar, c.seen & 1, abort, status)) return false;
-  return true;
-}
-
 __global__ void __launch_bounds__(kThreads, 1)
     attend_persistent_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                              const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ Params p) {
@@ -528,7 +532,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
-    for (int s = 0; s < kSlots; ++s) mbar_init(&sm.kv_full[s], 1);
+    for (int s = 0; s < kSlots; ++s) {
+      mbar_init(&sm.kv_full[s], 1);
+      mbar_init(&sm.kv_empty[s], 1);
+    }
+    mbar_init(&sm.q_empty, 1);
     for (int t = 0; t < 2; ++t) {
       mbar_init(&sm.s_full[t], 1);
       mbar_init(&sm.p_part[t][0], kSoftmaxWarps);
@@ -557,26 +565,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
     }
-    // Commit barriers and how many completions the issuer will have made on each before the
-    // current item: [0, 1] = s_full[t], [2, 3] = o_full[t].
-    CommitTrack track[4] = {{&sm.s_full[0], 0}, {&sm.s_full[1], 0}, {&sm.o_full[0], 0}, {&sm.o_full[1], 0}};
-    uint32_t made[4] = {0, 0, 0, 0};
-    // Release of the tile that last filled each ring slot: (commit barrier, completion index).
-    int rel_bar[kSlots];
-    uint32_t rel_idx[kSlots];
-    int q_rel_bar = -1;  // release of the Q tiles: the previous item's last S
-    uint32_t q_rel_idx = 0;
+    // Fill f of a buffer (the Q tiles, or a ring slot) waits for completion #(f-1) of its empty
+    // barrier; that barrier cannot complete again before fill f has landed and been read, so the
+    // parity wait always refers to its current or its previous phase.
     uint32_t g = 0, q_fills = 0;  // K/V loads and Q loads issued
     bool ok = true;
     for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x) {
       const Item it = decode_item(p, w);
-      const int sb = it.nt - 1, ob = 2 + it.nt - 1;  // barriers that release this item's tiles
-      const uint32_t base_s = made[sb], base_o = made[ob];
       const int row_base = it.bh * p.S;
-      // The Q tiles first: the previous item's last S is the latest completion any of this
-      // item's first loads needs, so the slot waits of K_0 and V_0 that follow return at once
-      // (and S(0) needs Q and K_0 together in any case).
-      if (q_rel_bar >= 0 && !await_completion(track[q_rel_bar], q_rel_idx, abort, p.status)) break;
+      if (q_fills > 0 && !mbar_wait_warp(&sm.q_empty, (q_fills - 1) & 1, abort, p.status)) break;
       if (leader) {
         mbar_arrive_expect_tx(&sm.q_full, it.nt * kTileBytes);
         for (int t = 0; t < it.nt; ++t) {
@@ -588,8 +585,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       ++q_fills;
       for (int n = 0; n < 2 * it.n_kv; ++n) {
-        const int slot = g % kSlots;
-        if (g >= kSlots && !await_completion(track[rel_bar[slot]], rel_idx[slot], abort, p.status)) {
+        const int slot = g % kSlots, fill = g / kSlots;
+        if (fill > 0 && !mbar_wait_warp(&sm.kv_empty[slot], (fill - 1) & 1, abort, p.status)) {
           ok = false;
           break;
         }
@@ -602,23 +599,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
         ++g;
-        const int b = n >> 1;
-        if (!(n & 1)) {
-          rel_bar[slot] = sb;  // K_b: read by S(b)
-          rel_idx[slot] = base_s + b;
-        } else if (b < it.n_kv - 1) {
-          rel_bar[slot] = sb;  // V_b: read by P.V(b), covered by the commit after S(b+1)
-          rel_idx[slot] = base_s + b + 1;
-        } else {
-          rel_bar[slot] = ob;  // the item's last V: covered by the o_full commit
-          rel_idx[slot] = base_o;
-        }
-      }
-      q_rel_bar = sb;
-      q_rel_idx = base_s + it.n_kv - 1;
-      for (int t = 0; t < it.nt; ++t) {
-        made[t] += it.n_kv;
-        made[2 + t] += 1;
       }
     }
     // Never leave with a copy in flight: wait (bounded) for the last fill of Q and of every slot.
@@ -658,6 +638,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_commit_warp(&sm.s_full[t]);
         }
       }
+      tc_commit_warp(&sm.kv_empty[g0 % kSlots]);  // K_0 has been read by every tile's S(0)
       for (int j = 0; ok && j < it.n_kv; ++j) {
         const uint32_t nv = g0 + 2 * j + 1, nk = g0 + 2 * j + 2;
         const bool last = (j == it.n_kv - 1);
@@ -682,6 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (!ok) break;
           if (last) {
+            if (t == it.nt - 1) tc_commit_warp(&sm.kv_empty[nv % kSlots]);  // the last V, read by every tile
             tc_commit_warp(&sm.o_full[t]);
             continue;
           }
@@ -706,16 +688,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t s_addr = tmem + lane_off + t * 128 + half * 64;
     const uint32_t o_addr = tmem + lane_off + 256 + t * 128 + half * 64;
     uint32_t s_seen = 0, o_seen = 0, items = 0;  // s_full[t] / o_full[t] completions consumed, items of tile t
+    uint32_t g0 = 0;                             // ring index of the item's first K/V load
     // Once a wait has failed the warp does no more work, but it still meets its tile's named
     // barrier once per item, as its partner warps (which may not have seen the failure yet) do.
     bool ok = true;
     for (int w = blockIdx.x; w < p.n_items; w += gridDim.x) {
       const Item it = decode_item(p, w);
+      const uint32_t item_g0 = g0;
+      g0 += 2 * it.n_kv;
       if (t >= it.nt) continue;
+      const bool releaser = t == it.nt - 1 && sw % kSoftmaxWarps == 0 && lane == 0;
       float2 l0 = make_float2(0.f, 0.f), l1 = make_float2(0.f, 0.f);
       for (int j = 0; ok && j < it.n_kv; ++j, ++s_seen) {
         ok = mbar_wait_warp(&sm.s_full[t], s_seen & 1, abort, p.status);
         if (!ok) break;
+        if (releaser) release_after_s(sm, item_g0, j, it.n_kv);
         tc_fence_after();
         uint32_t ra[32], rb[32], pk0[16], pk1[16];
         tmem_ld_32x32b_x32(s_addr, ra);
@@ -892,10 +879,9 @@ int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
   p.acc = splits > 1 ? static_cast<float*>(workspace) : nullptr;
   p.lsum = splits > 1 ? p.acc + static_cast<size_t>(splits) * rows * kDim : nullptr;
   p.status = status;
-  // The persistent form whenever the CTAs write plain output and every item has the same number
-  // of query tiles (its producer tracks one commit barrier per tile count); the one-item-per-CTA
-  // form for the TMA-staged epilogue, which borrows the Q buffers, and for odd tile counts.
-  const bool persistent = !p.tma_out && (p.n_tiles % 2 == 0 || p.n_tiles == 1);
+  // The persistent form whenever the CTAs write plain output; the one-item-per-CTA form for the
+  // TMA-staged epilogue, which borrows the Q buffers.
+  const bool persistent = !p.tma_out;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = persistent ? dim3(static_cast<unsigned>(std::min<long long>(items, sm_count[dev])))
                            : dim3(p.n_pairs, p.BH, splits);

@@ -3,13 +3,14 @@
 The kernel's three roles are restated as Python generators that yield their waits, in the same
 order and with the same completion indices as the CUDA code:
 
-* the producer (TMA warp): per item the Q tiles, then K_0, V_0, K_1, ... into a 4-slot ring,
-  each slot refilled once the commit that covers its previous tile's readers has completed,
-  awaited one completion at a time (``await_completion``);
+* the producer (TMA warp): per item the Q tiles, then K_0, V_0, K_1, ... into a 4-slot ring;
+  fill f of a buffer waits for completion #(f-1) of its empty barrier (q_empty, kv_empty[slot]);
 * the issuer (UMMA warp): S_t(0), then per KV block P.V_t(j) in two chunks and S_t(j+1), with
-  commits on s_full[t] and, after an item's last block, o_full[t];
+  commits on s_full[t] and, after an item's last block, on o_full[t];
 * 16 softmax warps: exp of S into P (two hand-over chunks), the row-sum exchange over a named
-  barrier (double-buffered by item parity) and the epilogue read of O.
+  barrier (double-buffered by item parity) and the epilogue read of O; one warp of the item's
+  last query tile releases the buffers inside an item (release_after_s) as it sees commits, the
+  issuer commits the releases of an item's first K and last V itself.
 
 The 'hardware' runs at random times: TMA copies land, UMMAs execute in issue order, commits
 arrive. mbarrier waits use the hardware's parity semantics (a wait for parity p returns once the
@@ -51,7 +52,7 @@ def decode(w, n_tiles, n_splits):
     return dict(w=w, nt=min(2, n_tiles - t0), n_kv=n_tiles * (split + 1) // n_splits - kv0)
 
 
-def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, step_completions=True):
+def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, release_from_tile0=False):
     n_items = bh * ((n_tiles + 1) // 2) * n_splits
     items = [decode(w, n_tiles, n_splits) for w in range(cta, n_items, grid)]
     q_full = Bar("q_full")
@@ -59,6 +60,8 @@ def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, step_completions=T
     s_full = [Bar(f"s_full{t}") for t in range(2)]
     p_part = [[Bar(f"p_part{t}{c}", 8) for c in range(2)] for t in range(2)]
     o_full = [Bar(f"o_full{t}") for t in range(2)]
+    kv_empty = [Bar(f"kv_empty{s}") for s in range(4)]
+    q_empty = Bar("q_empty")
     qbuf, q_inflight = [None, None], [False, False]
     kv, kv_inflight = [None] * 4, [False] * 4
     s_reg = [[[None] * 2 for _ in range(4)] for _ in range(2)]  # [tile][quad][half]
@@ -77,47 +80,25 @@ def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, step_completions=T
         return done
 
     def producer():
-        bars = [s_full[0], s_full[1], o_full[0], o_full[1]]
-        seen, made = [0] * 4, [0] * 4
-        rel, q_rel, g = [None] * 4, None, 0
-
-        def await_completion(bid, idx):
-            if step_completions:
-                while seen[bid] <= idx:
-                    yield ("wait", bars[bid], seen[bid])
-                    seen[bid] += 1
-            elif idx >= seen[bid]:  # planted mistake: jump straight to the wanted completion
-                yield ("wait", bars[bid], idx)
-                seen[bid] = idx + 1
-
+        g = q_fills = 0
         for it in items:
-            sb, ob = it["nt"] - 1, 2 + it["nt"] - 1
-            base_s, base_o = made[sb], made[ob]
-            if q_rel is not None:
-                yield from await_completion(*q_rel)
+            if q_fills > 0:
+                yield ("wait", q_empty, q_fills - 1)
+            if any(q_inflight):
+                raise ProtocolError("Q refilled while a copy into it is in flight")
             for t in range(it["nt"]):
                 q_inflight[t] = True
             tma.append(("q", it["w"], it["nt"]))
+            q_fills += 1
             for n in range(2 * it["n_kv"]):
-                slot = g % 4
-                if g >= 4:
-                    yield from await_completion(*rel[slot])
+                slot, fill = g % 4, g // 4
+                if fill > 0:
+                    yield ("wait", kv_empty[slot], fill - 1)
                 if kv_inflight[slot]:
                     raise ProtocolError("slot refilled while a copy into it is in flight")
                 kv_inflight[slot] = True
                 tma.append(("kv", slot, ("V" if n & 1 else "K", it["w"], n >> 1)))
                 g += 1
-                b = n >> 1
-                if not n & 1:
-                    rel[slot] = (sb, base_s + b)
-                elif b < it["n_kv"] - 1:
-                    rel[slot] = (sb, base_s + b + 1)
-                else:
-                    rel[slot] = (ob, base_o)
-            q_rel = (sb, base_s + it["n_kv"] - 1)
-            for t in range(it["nt"]):
-                made[t] += it["n_kv"]
-                made[2 + t] += 1
 
     def issuer():
         g0, done, blocks = 0, 0, [0, 0]
@@ -127,6 +108,7 @@ def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, step_completions=T
             for t in range(it["nt"]):
                 mma.append(("S", it["w"], t, 0, g0 % 4))
                 mma.append(("commit", s_full[t]))
+            mma.append(("commit", kv_empty[g0 % 4]))
             n_kv = it["n_kv"]
             for j in range(n_kv):
                 nv, nk = g0 + 2 * j + 1, g0 + 2 * j + 2
@@ -139,6 +121,8 @@ def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, step_completions=T
                         yield ("wait", p_part[t][c], blocks[t] + j)
                         mma.append(("PV", it["w"], t, j, c, nv % 4))
                     if last:
+                        if t == it["nt"] - 1:
+                            mma.append(("commit", kv_empty[nv % 4]))
                         mma.append(("commit", o_full[t]))
                     else:
                         mma.append(("S", it["w"], t, j + 1, nk % 4))
@@ -149,14 +133,24 @@ def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, step_completions=T
             done += 1
 
     def softmax(t, quad, half):
-        s_seen = o_seen = n_done = 0
+        s_seen = o_seen = n_done = g0 = 0
         for it in items:
+            item_g0 = g0
+            g0 += 2 * it["n_kv"]
             if t >= it["nt"]:
                 continue
             n_kv = it["n_kv"]
+            # planted mistake: releases made by tile 0's warp, whose commit does not cover tile 1
+            releaser = t == (0 if release_from_tile0 else it["nt"] - 1) and quad == 2 and half == 0
             for j in range(n_kv):
                 yield ("wait", s_full[t], s_seen)
                 s_seen += 1
+                if releaser:
+                    if j > 0:
+                        kv_empty[(item_g0 + 2 * j) % 4].arrive()
+                        kv_empty[(item_g0 + 2 * j - 1) % 4].arrive()
+                    if j == n_kv - 1:
+                        q_empty.arrive()
                 if s_reg[t][quad][half] != ("S", it["w"], t, j):
                     raise ProtocolError(f"softmax read S {s_reg[t][quad][half]}, wanted {('S', it['w'], t, j)}")
                 for c in range(2):
@@ -188,7 +182,7 @@ def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, step_completions=T
             if qbuf[t] != w or q_inflight[t]:
                 raise ProtocolError(f"S read Q {qbuf[t]} (copy in flight: {q_inflight[t]}), wanted {w}")
             if kv[slot] != ("K", w, j) or kv_inflight[slot]:
-                raise ProtocolError(f"S read K {kv[slot]}, wanted {('K', w, j)}")
+                raise ProtocolError(f"S read K {kv[slot]} (copy in flight: {kv_inflight[slot]}), wanted {('K', w, j)}")
             for quad in range(4):
                 for half in range(2):
                     s_reg[t][quad][half] = ("S", w, t, j)
@@ -196,7 +190,7 @@ def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, step_completions=T
         else:
             _, w, t, j, c, slot = e
             if kv[slot] != ("V", w, j) or kv_inflight[slot]:
-                raise ProtocolError(f"P.V read V {kv[slot]}, wanted {('V', w, j)}")
+                raise ProtocolError(f"P.V read V {kv[slot]} (copy in flight: {kv_inflight[slot]}), wanted {('V', w, j)}")
             for quad in range(4):
                 for half in range(2):
                     if p_reg[t][quad][half][c] != ("P", w, t, j):
@@ -257,10 +251,10 @@ def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, step_completions=T
     raise ProtocolError("no progress")
 
 
-# (tile count, KV splits, batch x heads, grid): the persistent kernel runs even tile counts and
-# single tiles, with and without KV splits, one or several items per CTA, single-block items.
-CASES = [(2, 1, 2, 1), (4, 1, 3, 2), (6, 4, 1, 1), (8, 3, 3, 2), (2, 2, 3, 1), (1, 1, 5, 2), (4, 4, 3, 2),
-         (6, 6, 2, 3), (10, 1, 2, 1)]
+# (tile count, KV splits, batch x heads, grid): even and odd tile counts (items of one and two
+# query tiles mixed), with and without KV splits, one or several items per CTA, single-block items.
+CASES = [(2, 1, 2, 1), (3, 1, 2, 1), (4, 1, 3, 2), (5, 1, 3, 2), (6, 4, 1, 1), (7, 2, 3, 2), (8, 3, 3, 2),
+         (2, 2, 3, 1), (3, 3, 2, 1), (1, 1, 5, 2), (4, 4, 3, 2), (6, 6, 2, 3), (9, 1, 2, 1), (10, 1, 2, 1)]
 
 
 @pytest.mark.parametrize("case", CASES)
@@ -273,10 +267,20 @@ def test_protocol_holds(case):
                 assert run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw) > 0
 
 
-def test_model_catches_a_skipped_completion():
-    """Planted in the model: a producer that waits for the completion it needs without stepping
-    through the ones before it (a parity wait two phases ahead returns at once)."""
+def test_model_catches_an_early_release():
+    """Planted in the model: buffers released by a warp of tile 0, whose s_full commit does not
+    cover tile 1's UMMAs, so a refill can land before tile 1 has read the old tile."""
     rng = random.Random(7)
-    with pytest.raises(ProtocolError):
-        for _ in range(50):
-            run_cta(2, 1, 3, 1, 0, rng, 0.3, step_completions=False)
+    with pytest.raises(ProtocolError, match="read"):
+        for _ in range(200):
+            run_cta(4, 1, 3, 1, 0, rng, 0.5, release_from_tile0=True)
+
+
+@pytest.mark.parametrize("case", [(4, 1, 3, 1), (5, 2, 2, 1)])
+def test_waits_never_fall_behind_under_any_schedule(case):
+    """Fully random scheduling (a copy or UMMA as likely as a ready warp): the empty barriers
+    make every parity wait unambiguous however late a warp runs."""
+    n_tiles, n_splits, bh, grid = case
+    rng = random.Random(11)
+    for _ in range(40):
+        run_cta(n_tiles, n_splits, bh, grid, 0, rng, 1.0)
