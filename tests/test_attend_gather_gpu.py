@@ -62,10 +62,11 @@ def test_shards_gathered_into_every_buffer(b, h, s, shards):
     assert err <= 2e-2
 
 
-# Even tile counts run the persistent kernel for attend_merged, while a gathering call into two
-# local buffers runs the one-item-per-CTA kernel with its TMA-staged epilogue: (1, 24, 4608) is
-# 432 items on 148 CTAs, (2, 24, 1536) 288 items, (3, 2, 128) single-tile items.
-@pytest.mark.parametrize("b,h,s", [(1, 24, 4608), (2, 24, 1536), (3, 2, 128), (1, 16, 2048)])
+# attend_merged runs the persistent kernel, while a gathering call into two local buffers runs
+# the one-item-per-CTA kernel with its TMA-staged epilogue: (1, 24, 4608) is 432 items on 148
+# CTAs, (2, 24, 1536) 288 items, (3, 2, 128) single-tile items, (2, 24, 1152) nine tiles per head
+# (items of two and of one query tile mixed).
+@pytest.mark.parametrize("b,h,s", [(1, 24, 4608), (2, 24, 1536), (3, 2, 128), (1, 16, 2048), (2, 24, 1152)])
 def test_attend_persistent_matches(b, h, s):
     """The persistent kernel (items walked by one CTA per SM, barriers counting across items)
     computes exactly what one CTA per item computes: bit-identical outputs."""
