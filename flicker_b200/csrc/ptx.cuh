@@ -127,73 +127,6 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, v
   return __all_sync(0xffffffffu, mbar_wait_slow(bar, parity, abort, status)) != 0;
 }
 
-// Non-blocking test of a phase (mbarrier.test_wait: returns at once, never suspends).
-__device__ __forceinline__ bool mbar_test_now(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// mbar_wait_warp for a warp whose wake-up latency is on the critical path: the lanes spin on
-// non-blocking tests instead of sleeping in try_wait (a sleeping waiter resumes a few hundred
-// cycles after the phase completes). Bounded as mbar_wait: the abort flag is read every poll, the
-// status word and the clock every kSpinPollsPerCheck polls.
-constexpr uint32_t kSpinPollsPerCheck = 4096;
-static __device__ __noinline__ bool mbar_spin_slow(uint64_t* bar, uint32_t parity, volatile int* abort, int* status) {
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t spin = 1; spin < kWaitSpinCap; ++spin) {
-    if (__all_sync(0xffffffffu, mbar_test_now(bar, parity))) return true;
-    if (*abort) return false;
-    if (spin % kSpinPollsPerCheck == 0) {
-      if (*reinterpret_cast<volatile int*>(status) != 0) {
-        *abort = 1;
-        return false;
-      }
-      if (globaltimer_ns() - t0 > kWaitLimitNs) break;
-    }
-  }
-  *abort = 1;
-  atomicExch(status, kErrDeviceTimeout);
-  return false;
-}
-__device__ __forceinline__ bool mbar_spin_warp(uint64_t* bar, uint32_t parity, volatile int* abort, int* status) {
-  if (__all_sync(0xffffffffu, mbar_test_now(bar, parity))) return true;
-  return __all_sync(0xffffffffu, mbar_spin_slow(bar, parity, abort, status)) != 0;
-}
-
-// As mbar_spin_warp, with a short sleep between polls: a wake-up within about kNapNs of the
-// phase completing, at a small fraction of the issue slots a tight spin takes from the warps
-// sharing the scheduler.
-constexpr uint32_t kNapNs = 32;
-static __device__ __noinline__ bool mbar_nap_slow(uint64_t* bar, uint32_t parity, volatile int* abort, int* status) {
-  const uint64_t t0 = globaltimer_ns();
-  for (uint32_t spin = 1; spin < kWaitSpinCap; ++spin) {
-    __nanosleep(kNapNs);
-    if (__all_sync(0xffffffffu, mbar_test_now(bar, parity))) return true;
-    if (*abort) return false;
-    if (spin % kSpinPollsPerCheck == 0) {
-      if (*reinterpret_cast<volatile int*>(status) != 0) {
-        *abort = 1;
-        return false;
-      }
-      if (globaltimer_ns() - t0 > kWaitLimitNs) break;
-    }
-  }
-  *abort = 1;
-  atomicExch(status, kErrDeviceTimeout);
-  return false;
-}
-__device__ __forceinline__ bool mbar_nap_warp(uint64_t* bar, uint32_t parity, volatile int* abort, int* status) {
-  if (__all_sync(0xffffffffu, mbar_test_now(bar, parity))) return true;
-  return __all_sync(0xffffffffu, mbar_nap_slow(bar, parity, abort, status)) != 0;
-}
-
 // Named barrier `id` (1..15) over `count` threads (a multiple of 32).
 __device__ __forceinline__ void named_barrier_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
