@@ -135,14 +135,23 @@ __device__ __forceinline__ void exp_chunk(const uint32_t (&r)[32], uint32_t (&pk
 
 // Row sum of the bf16-ROUNDED P values of one chunk (kernels.py:124-125 sums fp32(bf16(exp(s)))),
 // done after P is in TMEM and handed to the issuer, i.e. off the softmax -> P.V critical path.
+// l += fp32(v) for both bf16 halves of a packed word, one mixed-precision add each (PTX
+// add.rn.f32.bf16: the bf16 operand widens exactly, one rounding), i.e. the same arithmetic as
+// widening the halves and adding them, in fewer instructions.
+__device__ __forceinline__ void add_bf16_halves(uint32_t w, float& lo_acc, float& hi_acc) {
+  asm("{\n\t.reg .b16 lo, hi;\n\tmov.b32 {lo, hi}, %2;\n\t"
+      "add.rn.f32.bf16 %0, lo, %0;\n\tadd.rn.f32.bf16 %1, hi, %1;\n\t}"
+      : "+f"(lo_acc), "+f"(hi_acc)
+      : "r"(w));
+}
+
 __device__ __forceinline__ void row_sum_chunk(const uint32_t (&pk)[16], float2& l0, float2& l1) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    const float2 rounded = make_float2(__uint_as_float(pk[i] << 16), __uint_as_float(pk[i] & 0xFFFF0000u));
     if (i & 1)
-      l1 = __fadd2_rn(l1, rounded);
+      add_bf16_halves(pk[i], l1.x, l1.y);
     else
-      l0 = __fadd2_rn(l0, rounded);
+      add_bf16_halves(pk[i], l0.x, l0.y);
   }
 }
 
