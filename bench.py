@@ -52,7 +52,7 @@ GRIDS = {"512": (32, 32), "1024": (64, 64), "2048": (128, 128)}
 # each kernel on a B200 at this bench's workload; the capture commands and the other counters are
 # in profiles/ (attend_1024.md, qk_prep_1024.md, w8a8_gemm_config4.md). Reported as the roofline's
 # `traffic` beside the algorithmic bytes; other configurations report null.
-NCU_TRAFFIC_BYTES = {"attend@1024": 89_296_128, "qk_prep@1024": 118_335_744, "w8a8_gemm@config4": 86_272_768}
+NCU_TRAFFIC_BYTES = {"attend@1024": 89_164_288, "qk_prep@1024": 118_335_744, "w8a8_gemm@config4": 86_272_768}
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
