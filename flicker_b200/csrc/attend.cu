@@ -6,14 +6,19 @@
 // There is no running max and hence no rescaling of acc: the accumulator stays in
 // tensor memory for the whole KV loop and is read exactly once, in the epilogue.
 //
-// One CTA owns two 128-row query tiles of one (batch, head) and walks all KV blocks
-// of 128 rows (or one KV split of them). Warp roles (576 threads, 1 CTA per SM):
-//   warp 0       TMA producer: Q tiles once, then K_j, V_j into a 4-slot ring of 32 KB slots
+// A work item is two 128-row query tiles of one (batch, head) and all KV blocks of 128 rows
+// (or one KV split of them). attend_persistent_kernel runs one CTA per SM over many items;
+// attend_kernel runs one item per CTA (kept for the TMA-staged gathering epilogue, which
+// borrows the Q buffers). Warp roles (576 threads, 1 CTA per SM):
+//   warp 0       TMA producer: the item's Q tiles, then K_j, V_j into a 4-slot ring of 32 KB
+//                slots; every fill waits on its buffer's empty barrier (one completion per fill)
 //   warp 1       TMEM allocator + UMMA issuer
 //   warps 2-17   softmax: 8 warps per query tile, two per TMEM lane quadrant, each owning 64 of
 //                the 128 columns of its 32 rows: exp + bf16 round, P written back to TMEM in two
 //                32-column chunks (each handed to the issuer with one arrival per warp), row
 //                sums; then the epilogue O / l -> bf16 -> global (or fp32 partials for a split).
+//                One of them also releases ring slots and Q as it sees the commits (see
+//                release_after_s).
 // The producer and issuer warps run converged: all 32 lanes walk the loop and wait on the
 // barriers with one warp-wide vote per wait; lane 0 issues the TMA loads and elect.sync picks
 // the lane that issues each UMMA and commit.
