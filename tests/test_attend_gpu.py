@@ -159,3 +159,33 @@ def test_split_kv_matches_unsplit(b, h, s):
     assert R.within_tolerance(a[:, :, rows], want)
     assert R.within_tolerance(p[:, :, rows], want)
     assert fb.device_status() == 0
+
+
+def test_many_calls_keep_status_and_results():
+    """A soak of back-to-back calls: every barrier wait inside the kernels must keep ending (a
+    wait that misses its phase ends only at its time limit and records a device timeout), and
+    every call must reproduce the first one's output. 1500 calls at the 1024^2 shape (432 work
+    items on 148 persistent CTAs), then mixed shapes: split over KV, odd tile counts, one tile."""
+    def device_qkv(b, h, s, seed):
+        g = torch.Generator(device="cuda")
+        g.manual_seed(seed)
+        q = (torch.randn(b, h, s, 128, generator=g, device="cuda") / math.sqrt(128)).to(torch.bfloat16)
+        k = torch.randn(b, h, s, 128, generator=g, device="cuda").to(torch.bfloat16)
+        v = torch.randn(b, h, s, 128, generator=g, device="cuda").to(torch.bfloat16)
+        return q, k, v
+
+    assert fb.device_status() == 0
+    q, k, v = device_qkv(1, 24, 4608, 21)
+    first = fb.attend(q, k, v)
+    same = torch.ones((), dtype=torch.bool, device="cuda")
+    for _ in range(1500):
+        same &= (fb.attend(q, k, v) == first).all()
+    assert bool(same)
+    assert fb.device_status() == 0
+    shapes = [device_qkv(1, 3, 4608, 22), device_qkv(2, 24, 1152, 23), device_qkv(3, 2, 128, 24)]
+    firsts = [fb.attend(*x) for x in shapes]
+    for i in range(1000):
+        x = shapes[i % 3]
+        same &= (fb.attend(*x) == firsts[i % 3]).all()
+    assert bool(same)
+    assert fb.device_status() == 0
