@@ -44,6 +44,14 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "attend TFLOP/s + qk_prep HBM GB/s @1024² (S=4608,H=24,D=128) vs roofline"
+
+
+def metric_for(config: str) -> str:
+    """The headline metric (BASELINE.json's, at 1024²), or the same metric named for another grid."""
+    if config == "1024":
+        return METRIC
+    rows, cols = GRIDS[config]
+    return f"attend TFLOP/s + qk_prep HBM GB/s @{config}² (S={NUM_TXT + rows * cols},H={NUM_HEADS},D={HEAD_DIM}) vs roofline"
 NUM_HEADS = 24
 HEAD_DIM = 128
 NUM_TXT = 512
@@ -276,7 +284,7 @@ def run_reference(args, rank, world):
     sample = (f"{steps_run} steps x 1 head of {NUM_HEADS} (batch 1, S={s}); plain-XLA path "
               f"(heads, rms_norm, apply_rope, sdpa) restated in torch fp32 on host cores")
     line = {
-        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": steps_run,
+        "metric": metric_for(args.config), "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": steps_run,
         "warmup": warm_run, "ms_per_step": 1e3 * total / len(times), "higher_is_better": True,
         "scaling": "weak" if args.shard == "batch" else "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "impl": "reference",
@@ -790,7 +798,7 @@ def main():
     line = None
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": K,
+            "metric": metric_for(args.config), "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": K,
             "warmup": max(3, args.warmup), "ms_per_step": elapsed_ms / K, "higher_is_better": True,
             "scaling": "weak" if (args.shard == "batch" or world == 1) else "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
