@@ -50,7 +50,13 @@ HEAD_DIM = 128
 
 def row_tile(length: int) -> int | None:
     """kernels.py:23-24: first row tile that divides ``length``, or None."""
-    return next((size for size in ROW_TILES if length % size == 0), None)
+    tile = _ROW_TILE.get(length, 0)
+    if tile == 0:
+        tile = _ROW_TILE[length] = next((size for size in ROW_TILES if length % size == 0), None)
+    return tile
+
+
+_ROW_TILE: dict[int, int | None] = {}
 
 
 def lane_pair(freqs: Array, q_gain: float = 1.0) -> Freqs:
@@ -78,6 +84,17 @@ def _stream(t: Array) -> int:
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
+def _device_call(t: Array, call):
+    """``call(stream)`` with ``t``'s device current and that device's current stream. The device
+    context is entered only when another device is current: the API's host cost per call is what
+    small shapes (and CUDA-graph-free serving loops) pay for every launch."""
+    idx = t.get_device()
+    if idx != torch.cuda.current_device():
+        with torch.cuda.device(idx):
+            return call(torch.cuda.current_stream().cuda_stream)
+    return call(torch.cuda.current_stream().cuda_stream)
+
+
 def _require_cuda_bf16(name: str, t: Array) -> None:
     if not isinstance(t, torch.Tensor) or not t.is_cuda:
         raise ValueError(f"{name} must be a CUDA tensor (this package has no CPU path)")
@@ -100,17 +117,18 @@ def _qk_prep_args(qkv: Array, q_scale: Array, k_scale: Array, freqs: Freqs, num_
     if head_dim != HEAD_DIM:
         raise ValueError(f"head_dim must be {HEAD_DIM}, got {head_dim}")
     cos, sin, q_gain = freqs
+    dev = qkv.get_device()
     for name, t in (("freqs.cos", cos), ("freqs.sin", sin)):
-        if not isinstance(t, torch.Tensor) or t.device != qkv.device or t.dtype != torch.float32:
+        if not isinstance(t, torch.Tensor) or t.get_device() != dev or t.dtype != torch.float32:
             raise ValueError(f"{name} must be a float32 tensor on {qkv.device}")
-        if tuple(t.shape) != (length, head_dim):
+        if t.shape != (length, head_dim):
             raise ValueError(f"{name} must be [L, {head_dim}] = [{length}, {head_dim}], got {tuple(t.shape)}")
     scales = []
     for name, t in (("q_scale", q_scale), ("k_scale", k_scale)):
         _require_cuda_bf16(name, t)
-        if t.numel() != head_dim or t.device != qkv.device:
+        if t.numel() != head_dim or t.get_device() != dev:
             raise ValueError(f"{name} must hold {head_dim} values on {qkv.device}")
-        scales.append(t.reshape(head_dim).contiguous())
+        scales.append(t if t.dim() == 1 and t.is_contiguous() else t.reshape(head_dim).contiguous())
     return qkv.contiguous(), scales, cos.contiguous(), sin.contiguous(), float(q_gain), batch, length, head_dim
 
 
@@ -137,13 +155,13 @@ def qk_prep(
         raise NotImplementedError("interpret=True: this build runs only the sm_100a kernels")
     qkv, scales, cos, sin, q_gain, batch, length, head_dim = _qk_prep_args(qkv, q_scale, k_scale, freqs,
                                                                           num_heads, rows)
-    out = [torch.empty((batch, num_heads, length, head_dim), dtype=qkv.dtype, device=qkv.device)
-           for _ in range(3)]
-    with torch.cuda.device(qkv.device):
-        code = _lib.lib().flk_qk_prep(
-            qkv.data_ptr(), scales[0].data_ptr(), scales[1].data_ptr(), cos.data_ptr(), sin.data_ptr(),
-            q_gain, batch, length, num_heads, head_dim,
-            out[0].data_ptr(), out[1].data_ptr(), out[2].data_ptr(), _stream(qkv))
+    # q, k, v as three views of one allocation (one call into the caching allocator)
+    out = torch.empty((3, batch, num_heads, length, head_dim), dtype=qkv.dtype, device=qkv.device).unbind(0)
+    lib = _lib.lib()
+    code = _device_call(qkv, lambda stream: lib.flk_qk_prep(
+        qkv.data_ptr(), scales[0].data_ptr(), scales[1].data_ptr(), cos.data_ptr(), sin.data_ptr(),
+        q_gain, batch, length, num_heads, head_dim,
+        out[0].data_ptr(), out[1].data_ptr(), out[2].data_ptr(), stream))
     _lib.check("flk_qk_prep", code)
     return out[0], out[1], out[2]
 
@@ -161,19 +179,20 @@ def qk_prep_into(qkv: Array, q_scale: Array, k_scale: Array, freqs: Freqs, num_h
     if len(out) != 3:
         raise ValueError("out must be the (q, k, v) buffers")
     seq = out[0].shape[2] if out[0].dim() == 4 else -1
+    dev = qkv.get_device()
     for name, t in zip("qkv", out):
         _require_cuda_bf16(f"out.{name}", t)
-        if (tuple(t.shape) != (batch, num_heads, seq, head_dim) or not t.is_contiguous()
-                or t.device != qkv.device):
+        if (t.shape != (batch, num_heads, seq, head_dim) or not t.is_contiguous()
+                or t.get_device() != dev):
             raise ValueError(f"out.{name} must be a contiguous [B, H, S, D] = [{batch}, {num_heads}, S, "
                              f"{head_dim}] tensor on {qkv.device}, got {tuple(t.shape)}")
     if row < 0 or row + length > seq:
         raise ValueError(f"rows [{row}, {row + length}) do not fit in S={seq}")
-    with torch.cuda.device(qkv.device):
-        code = _lib.lib().flk_qk_prep_into(
-            qkv.data_ptr(), scales[0].data_ptr(), scales[1].data_ptr(), cos.data_ptr(), sin.data_ptr(),
-            q_gain, batch, length, num_heads, head_dim,
-            out[0].data_ptr(), out[1].data_ptr(), out[2].data_ptr(), seq, row, _stream(qkv))
+    lib = _lib.lib()
+    code = _device_call(qkv, lambda stream: lib.flk_qk_prep_into(
+        qkv.data_ptr(), scales[0].data_ptr(), scales[1].data_ptr(), cos.data_ptr(), sin.data_ptr(),
+        q_gain, batch, length, num_heads, head_dim,
+        out[0].data_ptr(), out[1].data_ptr(), out[2].data_ptr(), seq, row, stream))
     _lib.check("flk_qk_prep_into", code)
 
 
@@ -196,17 +215,18 @@ def double_qk_prep(txt_qkv: Array, img_qkv: Array, txt_scales: tuple[Array, Arra
     if img_qkv.shape[0] != batch or img_qkv.shape[2] != width or num_heads <= 0 or width % (3 * num_heads):
         raise ValueError("txt_qkv and img_qkv must share batch and width 3 * num_heads * head_dim")
     head_dim = width // (3 * num_heads)
-    out = tuple(torch.empty((batch, num_heads, num_txt + num_img, head_dim), dtype=txt_qkv.dtype,
-                            device=txt_qkv.device) for _ in range(3))
+    out = torch.empty((3, batch, num_heads, num_txt + num_img, head_dim), dtype=txt_qkv.dtype,
+                      device=txt_qkv.device).unbind(0)
     qk_prep_into(txt_qkv, *txt_scales, Freqs(cos[:num_txt], sin[:num_txt], q_gain), num_heads, out, 0)
     qk_prep_into(img_qkv, *img_scales, Freqs(cos[num_txt:], sin[num_txt:], q_gain), num_heads, out, num_txt)
     return out
 
 
 def _attend_args(q: Array, k: Array, v: Array, block: int | None):
+    dev = q.get_device() if isinstance(q, torch.Tensor) else None
     for name, t in (("q", q), ("k", k), ("v", v)):
         _require_cuda_bf16(name, t)
-        if t.dim() != 4 or tuple(t.shape) != tuple(q.shape) or t.device != q.device:
+        if t.dim() != 4 or t.shape != q.shape or t.get_device() != dev:
             raise ValueError(f"q, k, v must share one [B, H, S, D] shape and device; {name} is "
                              f"{tuple(t.shape)}")
     batch, heads, length, dim = q.shape
@@ -219,15 +239,26 @@ def _attend_args(q: Array, k: Array, v: Array, block: int | None):
     return q.contiguous(), k.contiguous(), v.contiguous(), batch, heads, length, dim
 
 
+# Workspace bytes of a split-KV call, per (device, B, H, S): a function of the shape and the
+# device's SM count only, so it is asked of the library once per shape.
+_WS_BYTES: dict[tuple[int, int, int, int], int] = {}
+
+
 def _run_attend(fn: str, q: Array, k: Array, v: Array, o: Array, batch: int, heads: int, length: int,
                 dim: int) -> Array:
     lib = _lib.lib()
-    with torch.cuda.device(q.device):
-        ws_bytes = lib.flk_attend_workspace_size(batch, heads, length, dim)
+    entry = getattr(lib, fn)
+
+    def call(stream: int) -> int:
+        key = (q.get_device(), batch, heads, length)
+        ws_bytes = _WS_BYTES.get(key)
+        if ws_bytes is None:
+            ws_bytes = _WS_BYTES[key] = lib.flk_attend_workspace_size(batch, heads, length, dim)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
-        code = getattr(lib, fn)(q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, length, dim,
-                                o.data_ptr(), ws.data_ptr() if ws is not None else None, ws_bytes, _stream(q))
-    _lib.check(fn, code)
+        return entry(q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, length, dim,
+                     o.data_ptr(), ws.data_ptr() if ws is not None else None, ws_bytes, stream)
+
+    _lib.check(fn, _device_call(q, call))
     return o
 
 

@@ -17,7 +17,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from .kernels import HEAD_DIM, Freqs, _require_cuda_bf16, _stream
+from .kernels import HEAD_DIM, Freqs, _device_call, _require_cuda_bf16
 
 Array = torch.Tensor
 
@@ -47,8 +47,8 @@ def linear(x: Array, wt: Array) -> Array:
     x2, m, n, k = _check_xw(x, wt)
     wt = wt.contiguous()
     y = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
-    with torch.cuda.device(x.device):
-        code = _lib.lib().flk_linear(x2.data_ptr(), wt.data_ptr(), m, n, k, y.data_ptr(), _stream(x))
+    lib = _lib.lib()
+    code = _device_call(x2, lambda stream: lib.flk_linear(x2.data_ptr(), wt.data_ptr(), m, n, k, y.data_ptr(), stream))
     _lib.check("flk_linear", code)
     return y.reshape(*x.shape[:-1], n)
 
@@ -94,10 +94,10 @@ def qkv_projection(x: Array, wt: Array, q_scale: Array, k_scale: Array, freqs: F
         raise ValueError(f"rows [{row}, {row + length}) do not fit in S={seq}")
     rest = torch.empty((m, n - n_qkv), dtype=torch.bfloat16, device=x.device) if n > n_qkv else None
     cos, sin, wt = cos.contiguous(), sin.contiguous(), wt.contiguous()
-    with torch.cuda.device(x.device):
-        code = _lib.lib().flk_linear_qk_prep(
-            x2.data_ptr(), wt.data_ptr(), m, n, k, scales[0].data_ptr(), scales[1].data_ptr(), cos.data_ptr(),
-            sin.data_ptr(), float(q_gain), batch, length, num_heads, HEAD_DIM, out[0].data_ptr(), out[1].data_ptr(),
-            out[2].data_ptr(), seq, row, rest.data_ptr() if rest is not None else None, _stream(x))
+    lib = _lib.lib()
+    code = _device_call(x2, lambda stream: lib.flk_linear_qk_prep(
+        x2.data_ptr(), wt.data_ptr(), m, n, k, scales[0].data_ptr(), scales[1].data_ptr(), cos.data_ptr(),
+        sin.data_ptr(), float(q_gain), batch, length, num_heads, HEAD_DIM, out[0].data_ptr(), out[1].data_ptr(),
+        out[2].data_ptr(), seq, row, rest.data_ptr() if rest is not None else None, stream))
     _lib.check("flk_linear_qk_prep", code)
     return out[0], out[1], out[2], (rest.reshape(batch, length, n - n_qkv) if rest is not None else None)

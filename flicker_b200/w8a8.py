@@ -16,6 +16,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
+from .kernels import _device_call
 
 ALPHA = 0.5
 
@@ -56,9 +57,9 @@ def quantize_act(x: torch.Tensor, inv_s: torch.Tensor):
     x, inv_s = x.contiguous(), inv_s.contiguous()
     xq = torch.empty((m, k), dtype=torch.int8, device=x.device)
     sx = torch.empty((m,), dtype=torch.float32, device=x.device)
-    with torch.cuda.device(x.device):
-        code = _lib.lib().flk_w8a8_quantize_act(x.data_ptr(), inv_s.data_ptr(), m, k, xq.data_ptr(),
-                                                sx.data_ptr(), _stream(x))
+    lib = _lib.lib()
+    code = _device_call(x, lambda stream: lib.flk_w8a8_quantize_act(x.data_ptr(), inv_s.data_ptr(), m, k,
+                                                                    xq.data_ptr(), sx.data_ptr(), stream))
     _lib.check("flk_w8a8_quantize_act", code)
     return xq, sx
 
@@ -72,10 +73,10 @@ def gemm(xq: torch.Tensor, wq: torch.Tensor, x_scale: torch.Tensor, w_scale: tor
     if wq.shape[1] != k or k % 16:
         raise ValueError(f"wq must be [N, K={k}] and K must be a multiple of 16")
     y = torch.empty((m, n), dtype=torch.bfloat16, device=xq.device)
-    with torch.cuda.device(xq.device):
-        code = _lib.lib().flk_w8a8_gemm(xq.contiguous().data_ptr(), wq.contiguous().data_ptr(),
-                                        x_scale.contiguous().data_ptr(), w_scale.contiguous().data_ptr(),
-                                        m, n, k, y.data_ptr(), _stream(xq))
+    xq, wq, x_scale, w_scale = xq.contiguous(), wq.contiguous(), x_scale.contiguous(), w_scale.contiguous()
+    lib = _lib.lib()
+    code = _device_call(xq, lambda stream: lib.flk_w8a8_gemm(xq.data_ptr(), wq.data_ptr(), x_scale.data_ptr(),
+                                                             w_scale.data_ptr(), m, n, k, y.data_ptr(), stream))
     _lib.check("flk_w8a8_gemm", code)
     return y
 
