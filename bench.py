@@ -76,6 +76,9 @@ def parse_args():
                     help="--shard heads: epilogue stores into every rank's buffer, or an NCCL all-gather")
     ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end leg (default K/10)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--graph", action="store_true",
+                    help="attention workload, one GPU or batch sharding: also time the step replayed from a "
+                         "captured CUDA graph (key `graph`; the headline stays the eager API path)")
     ap.add_argument("--cpu-heads", type=int, default=4, help="heads in the CPU-baseline sample")
     ap.add_argument("--workload", choices=["attention", "w8a8", "double", "projection"], default="attention",
                     help="attention: qk_prep + attend (the headline); w8a8: the SmoothQuant linear of config 4; "
@@ -752,6 +755,42 @@ def main():
         elapsed_ms = float(t.item())
     status = fb.device_status()
 
+    # ---- optional: the same step replayed from CUDA graphs (one per input set), without the
+    # API's per-call host cost; the eager calls above are the headline
+    graph_line = None
+    if args.graph and peer is None and gathered is None:
+        graphs = []
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for i in range(2):
+                step(i)
+        torch.cuda.current_stream().wait_stream(side)
+        for i in range(2):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                step(i)
+            graphs.append(gr)
+        for i in range(max(3, args.warmup)):
+            graphs[i % 2].replay()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        g0.record()
+        for i in range(K):
+            graphs[i % 2].replay()
+        g1.record()
+        torch.cuda.synchronize()
+        graph_ms = g0.elapsed_time(g1)
+        if world > 1:
+            t = torch.tensor([graph_ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            graph_ms = float(t.item())
+        graph_line = {"ms_per_step": graph_ms / K, "launches_per_step": 2}
+        del graphs
+        status = status or fb.device_status()
+
     # ---- end-to-end leg: host buffers through the public API, copies inside the timed region
     e2e_steps = args.e2e_steps or max(3, K // 10)
     qkv0, qs0, ks0, freqs0 = sets[0]
@@ -839,6 +878,10 @@ def main():
             "clocks": clocks.summary,
             "device_status": status,
         }
+        if graph_line is not None:
+            graph_line["value"] = total_flops / (graph_line["ms_per_step"] * 1e-3) / 1e12
+            graph_line["unit"] = "TFLOP/s"
+            line["graph"] = graph_line
     if world > 1:
         peer = None  # release the symmetric-memory buffers before the group goes away
         dist.barrier()
