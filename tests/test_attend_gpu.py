@@ -189,3 +189,18 @@ def test_many_calls_keep_status_and_results():
         same &= (fb.attend(*x) == firsts[i % 3]).all()
     assert bool(same)
     assert fb.device_status() == 0
+
+
+def test_empty_inputs_give_empty_outputs():
+    """Zero batch, zero-length sequences: no launch, empty results of the right shapes."""
+    for shape in ((1, 2, 0, 128), (0, 2, 256, 128)):
+        q = torch.empty(shape, dtype=torch.bfloat16, device="cuda")
+        assert fb.attend(q, q, q).shape == shape
+        assert fb.attend_merged(q, q, q).shape == (shape[0], shape[2], shape[1] * 128)
+    scale = torch.ones(128, dtype=torch.bfloat16, device="cuda")
+    for b, length in ((1, 0), (0, 512)):
+        qkv = torch.empty((b, length, 3 * 2 * 128), dtype=torch.bfloat16, device="cuda")
+        tab = torch.zeros((length, 128), dtype=torch.float32, device="cuda")
+        q, k, v = fb.qk_prep(qkv, scale, scale, fb.Freqs(tab, tab, 1.0), 2)
+        assert q.shape == k.shape == v.shape == (b, 2, length, 128)
+    assert fb.device_status() == 0
