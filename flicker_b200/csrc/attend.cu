@@ -811,16 +811,35 @@ static EncodeTiledFn get_encode_fn() {
 }
 
 // [rows, 128] bf16 row-major viewed through 64-column x 128-row boxes with the 128-byte swizzle.
+// Such a descriptor depends on nothing but (base, rows), so the last few are kept per host thread
+// and a caller that reuses its buffers skips the driver's encoding on later calls.
+struct TileMapEntry {
+  const void* base;
+  long long rows;
+  CUtensorMap map;
+};
 static bool make_tile_map(CUtensorMap* map, const void* base, long long rows) {
+  constexpr int kEntries = 8;
+  thread_local TileMapEntry cache[kEntries] = {};
+  thread_local int next = 0;
+  for (const TileMapEntry& e : cache)
+    if (e.base == base && e.rows == rows && base != nullptr) {
+      *map = e.map;
+      return true;
+    }
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return false;
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(kDim), static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(kDim) * 2};
   const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kTile)};
   const cuuint32_t estr[2] = {1, 1};
-  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  if (enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  cache[next] = TileMapEntry{base, rows, *map};
+  next = (next + 1) % kEntries;
+  return true;
 }
 
 // Output map for the staged epilogue: [B*S rows, H_out*128 cols] bf16, 64 x 32 boxes, 128-byte swizzle.
