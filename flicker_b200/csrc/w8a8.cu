@@ -255,6 +255,27 @@ __device__ __forceinline__ int quant_code(float xs, float scale, float inv) {
   return max(-127, min(127, q));
 }
 
+// quant_code for two values at once, with the same roundings done by packed float2 operations
+// (two round-to-nearest results per instruction): r = rn(x' * inv), t = rn(r + 1.5 * 2^23),
+// rint(r) = t - 1.5 * 2^23 and r - rint(r) (both exact).
+__device__ __forceinline__ void quant_codes2(float2 xs, float scale, float inv, int& q0, int& q1) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23, bit pattern 0x4B400000
+  constexpr float kLimit = 0.5f - 6.103515625e-05f;
+  const float2 r = __fmul2_rn(xs, make_float2(inv, inv));
+  const float2 t = __fadd2_rn(r, make_float2(kRound, kRound));
+  const float2 n = __fadd2_rn(t, make_float2(-kRound, -kRound));
+  const float2 d = __ffma2_rn(n, make_float2(-1.0f, -1.0f), r);
+  q0 = fabsf(d.x) < kLimit ? __float_as_int(t.x) - 0x4B400000 : __float2int_rn(__fdiv_rn(xs.x, scale));
+  q1 = fabsf(d.y) < kLimit ? __float_as_int(t.y) - 0x4B400000 : __float2int_rn(__fdiv_rn(xs.y, scale));
+  q0 = max(-127, min(127, q0));
+  q1 = max(-127, min(127, q1));
+}
+
+// The low bytes of four codes as one word, code 0 in the lowest byte.
+__device__ __forceinline__ uint32_t pack_codes4(int q0, int q1, int q2, int q3) {
+  return __byte_perm(__byte_perm(q0, q1, 0x0040), __byte_perm(q2, q3, 0x0040), 0x5410);
+}
+
 // One warp per row: x' = float(x) * inv_smooth, absmax over the row, scale = absmax / 127,
 // q = clamp(rint(x' / scale), -127, 127). K % 8 == 0 (16-byte vectors).
 __global__ void __launch_bounds__(256) quantize_act_kernel(const uint16_t* __restrict__ x,
@@ -321,7 +342,7 @@ __global__ void __launch_bounds__(kRowThreads) quantize_act_row_kernel(const uin
     const int c = (it * kRowThreads + tid) * 8;
     v[it] = c < K ? *reinterpret_cast<const uint4*>(xr + c) : make_uint4(0, 0, 0, 0);
   }
-  float xs[kIters][8];
+  float2 xs[kIters][4];  // x' in pairs: columns (2p, 2p+1) of the thread's 8
   float amax = 0.f;
 #pragma unroll
   for (int it = 0; it < kIters; ++it) {
@@ -332,12 +353,13 @@ __global__ void __launch_bounds__(kRowThreads) quantize_act_row_kernel(const uin
       s1 = __ldg(reinterpret_cast<const float4*>(inv_s + c + 4));
     }
     const uint32_t w[4] = {v[it].x, v[it].y, v[it].z, v[it].w};
-    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const float2 sv[4] = {make_float2(s0.x, s0.y), make_float2(s0.z, s0.w), make_float2(s1.x, s1.y),
+                          make_float2(s1.z, s1.w)};
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float xv = (j & 1) ? __uint_as_float(w[j >> 1] & 0xFFFF0000u) : __uint_as_float(w[j >> 1] << 16);
-      xs[it][j] = __fmul_rn(xv, sv[j]);
-      amax = fmaxf(amax, fabsf(xs[it][j]));
+    for (int p = 0; p < 4; ++p) {
+      const float2 xv = make_float2(__uint_as_float(w[p] << 16), __uint_as_float(w[p] & 0xFFFF0000u));
+      xs[it][p] = __fmul2_rn(xv, sv[p]);
+      amax = fmaxf(amax, fmaxf(fabsf(xs[it][p].x), fabsf(xs[it][p].y)));
     }
   }
 #pragma unroll
@@ -355,11 +377,11 @@ __global__ void __launch_bounds__(kRowThreads) quantize_act_row_kernel(const uin
   for (int it = 0; it < kIters; ++it) {
     const int c = (it * kRowThreads + tid) * 8;
     if (c >= K) break;
-    uint32_t packed[2] = {0u, 0u};
+    int q[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      packed[j >> 2] |= (static_cast<uint32_t>(quant_code(xs[it][j], scale, inv)) & 0xFFu) << (8 * (j & 3));
-    *reinterpret_cast<uint2*>(qr + c) = make_uint2(packed[0], packed[1]);
+    for (int p = 0; p < 4; ++p) quant_codes2(xs[it][p], scale, inv, q[2 * p], q[2 * p + 1]);
+    *reinterpret_cast<uint2*>(qr + c) =
+        make_uint2(pack_codes4(q[0], q[1], q[2], q[3]), pack_codes4(q[4], q[5], q[6], q[7]));
   }
 }
 
