@@ -57,10 +57,15 @@ HEAD_DIM = 128
 NUM_TXT = 512
 GRIDS = {"512": (32, 32), "1024": (64, 64), "2048": (128, 128)}
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch from one ncu capture of
-# each kernel on a B200 at this bench's workload; the capture commands and the other counters are
-# in profiles/ (attend_1024.md, qk_prep_1024.md, w8a8_gemm_config4.md). Reported as the roofline's
-# `traffic` beside the algorithmic bytes; other configurations report null.
+# each kernel on a B200 at this bench's workload (the capture commands and the other counters are
+# kept with the profile summaries). Reported as the roofline's `traffic` beside the algorithmic
+# bytes; other configurations report null. A captured launch writes its outputs into L2, and the
+# part still dirty in L2 when it ends is written back during later launches, so an HBM-bound
+# kernel's figure can sit below its algorithmic bytes.
 NCU_TRAFFIC_BYTES = {"attend@1024": 89_164_288, "qk_prep@1024": 118_335_744, "w8a8_gemm@config4": 86_272_768}
+NCU_TRAFFIC_NOTE = "ncu dram__bytes_read.sum + dram__bytes_write.sum of one captured launch at this workload"
+E2E_MIN_STEPS = 20  # the end-to-end leg times at least this many steps whatever --steps is
+CPU_WARMUP, CPU_RUNS = 3, 20  # CPU baseline: median of >= 20 timed runs after 3 warm-ups
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
@@ -74,12 +79,14 @@ def parse_args():
     ap.add_argument("--shard", choices=["batch", "heads"], default="batch")
     ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
                     help="--shard heads: epilogue stores into every rank's buffer, or an NCCL all-gather")
-    ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end leg (default K/10)")
+    ap.add_argument("--e2e-steps", type=int, default=None,
+                    help=f"steps of the end-to-end leg (default max({E2E_MIN_STEPS}, K/10))")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--graph", action="store_true",
                     help="attention workload, one GPU or batch sharding: also time the step replayed from a "
                          "captured CUDA graph (key `graph`; the headline stays the eager API path)")
-    ap.add_argument("--cpu-heads", type=int, default=4, help="heads in the CPU-baseline sample")
+    ap.add_argument("--no-heads-sharded", action="store_true",
+                    help="N > 1: skip the head-sharded batch-1 measurement added to the line as `heads_sharded`")
     ap.add_argument("--workload", choices=["attention", "w8a8", "double", "projection"], default="attention",
                     help="attention: qk_prep + attend (the headline); w8a8: the SmoothQuant linear of config 4; "
                          "double: a double block's attention section with the fused concat and merged heads; "
@@ -249,8 +256,14 @@ def make_inputs(torch, config, batch, heads, seed, device):
 
 
 # ------------------------------------------------------------------ reference arm / CPU leg
-def cpu_sample(config, n_heads, reps=1):
-    """Time the CPU restatement of the reference's XLA path on `n_heads` heads of `config`."""
+def cpu_measure(config, warmup=CPU_WARMUP, runs=CPU_RUNS):
+    """Time the CPU restatement of the reference's plain-XLA path on `config`, one head per run.
+
+    The reference's own convention (tools/bench.py:21,25-33 of flicker): untimed warm-ups, then
+    the median of the timed runs. Run r covers head r % 24 of the batch-1 call, so every run is
+    the same amount of work; the value is that head's attend FLOPs over the median time. Used
+    by both the `cpu_baseline` leg of our arm and the reference arm, so the two agree.
+    """
     import torch
 
     from oracle import cpu_baseline, restatement as R
@@ -263,37 +276,36 @@ def cpu_sample(config, n_heads, reps=1):
     k_scale = torch.from_numpy(ks.view("int16")).view(torch.bfloat16)
     pe = torch.from_numpy(R.joint_pe(gh, gw))
     times, flops, threads = [], 0.0, 1
-    for r in range(reps):
-        h0 = (r * n_heads) % NUM_HEADS
-        heads = range(h0, min(NUM_HEADS, h0 + n_heads))
-        dt, fl, threads = cpu_baseline.time_heads(qkv, q_scale, k_scale, pe, NUM_HEADS, heads)
-        times.append(dt)
-        flops = fl
-    return times, flops, threads, s
+    for r in range(warmup + runs):
+        h = r % NUM_HEADS
+        dt, flops, threads = cpu_baseline.time_heads(qkv, q_scale, k_scale, pe, NUM_HEADS, range(h, h + 1))
+        if r >= warmup:
+            times.append(dt)
+    med = statistics.median(times)
+    return {"value": flops / med / 1e12, "ms_median": med * 1e3, "runs": runs, "warmup": warmup,
+            "cores": threads, "seq_len": s,
+            "sample": f"1 of {NUM_HEADS} heads per run (batch 1, S={s}), median of {runs} runs after {warmup} "
+                      f"warm-ups; plain-XLA path (heads, rms_norm, apply_rope, sdpa) restated in torch fp32 "
+                      f"on {threads} host threads"}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
-    n_heads = 1
-    steps, warmup = max(1, args.steps), max(0, args.warmup)
-    # Bound the arm to a few minutes: one head per step, at most 40 timed steps.
-    steps_run = min(steps, 40)
-    warm_run = min(warmup, 3)
-    cpu_sample(args.config, n_heads, reps=warm_run) if warm_run else None
-    times, flops, threads, s = cpu_sample(args.config, n_heads, reps=steps_run)
-    total = sum(times)
-    value = flops * len(times) / total / 1e12
-    sample = (f"{steps_run} steps x 1 head of {NUM_HEADS} (batch 1, S={s}); plain-XLA path "
-              f"(heads, rms_norm, apply_rope, sdpa) restated in torch fp32 on host cores")
+    # Bounded to well under a minute: one head per run, at least 20 and at most 200 timed runs.
+    runs = min(max(args.steps, CPU_RUNS), 200)
+    warmup = min(max(args.warmup, CPU_WARMUP), 20)
+    m = cpu_measure(args.config, warmup=warmup, runs=runs)
+    value = m["value"]
     line = {
-        "metric": metric_for(args.config), "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": steps_run,
-        "warmup": warm_run, "ms_per_step": 1e3 * total / len(times), "higher_is_better": True,
+        "metric": metric_for(args.config), "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": runs,
+        "warmup": warmup, "ms_per_step": m["ms_median"], "higher_is_better": True,
         "scaling": "weak" if args.shard == "batch" else "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "impl": "reference",
         "config": {"workload": f"flicker {args.config}^2 attention call: qk_prep + attend", "batch": 1,
-                   "seq_len": s, "heads": NUM_HEADS, "head_dim": HEAD_DIM},
-        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
+                   "seq_len": m["seq_len"], "heads": NUM_HEADS, "head_dim": HEAD_DIM},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": m["cores"], "kind": "port",
+                         "sample": m["sample"]},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -329,6 +341,7 @@ def run_w8a8(args, rank, world):
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
         torch.cuda.synchronize()
+        preroll(torch)
         start.record()
         for i in range(steps):
             e = ev_q[i]
@@ -345,11 +358,11 @@ def run_w8a8(args, rank, world):
     ops = 2.0 * M * N * K
     # end to end through the layer: X from pinned host memory, y back to pinned host memory
     pipe = CopyPipeline(torch, [sets[0].cpu().pin_memory()], (M, N), torch.bfloat16)
-    e2e_steps = args.e2e_steps or max(3, steps // 10)
+    e2e_steps = args.e2e_steps or max(E2E_MIN_STEPS, steps // 10)
     pipe.run(2, lambda d: layer(d[0]))
     e2e_ms = pipe.run(e2e_steps, lambda d: layer(d[0]))
     pk, pk_kind = peaks()
-    int8_peak = 2.0 * pk["bf16_tflops"]  # no measured int8 peak: twice the measured bf16 GEMM
+    int8_peak, int8_clocks = measure_int8_peak(torch, local_rank)
     gemm_tops = ops / (g_us * 1e-6) / 1e12
     line = {
         "metric": "W8A8 SmoothQuant linear TOPS @[4608x3072]x[3072x9216] (config 4)",
@@ -363,8 +376,11 @@ def run_w8a8(args, rank, world):
                     "w8a8_gemm": {"us": g_us, "TOPS": gemm_tops}},
         "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": int8_peak, "unit": "TOPS",
                      "frac": gemm_tops / int8_peak, "traffic": NCU_TRAFFIC_BYTES["w8a8_gemm@config4"],
-                     "traffic_source": "ncu capture, profiles/w8a8_gemm_config4.md", "kernel": "w8a8_gemm",
-                     "peak_source": f"2 x {pk_kind} bf16 burst (no measured int8 peak); nominal dense int8 4500"},
+                     "traffic_source": NCU_TRAFFIC_NOTE, "kernel": "w8a8_gemm",
+                     "peak_source": "measured here: torch._int_mm (cuBLASLt int8) 8192^3, best of 10, CUDA "
+                                    "events; nominal dense int8 4500",
+                     "peak_clocks": int8_clocks,
+                     "frac_2x_bf16_burst": gemm_tops / (2.0 * pk["bf16_tflops"])},
         "e2e": {"value": ops / (e2e_ms * 1e-3) / 1e12, "unit": "TOPS", "h2d_bytes_per_step": pipe.h2d_bytes,
                 "d2h_bytes_per_step": pipe.d2h_bytes, "steps": e2e_steps, "ms_per_step": e2e_ms},
         "gpu_launches": 2 * steps, "clocks": clocks.summary, "device_status": _lib.lib().flk_device_status(),
@@ -374,6 +390,30 @@ def run_w8a8(args, rank, world):
     if rank == 0:
         print(json.dumps(line), flush=True)
     return 0
+
+
+def measure_int8_peak(torch, gpu_index):
+    """Dense int8 tensor-core throughput of a library GEMM on this GPU: torch._int_mm (cuBLASLt)
+    at 8192^3, 2 * 8192^3 ops per call, best of 10 calls after 3 warm-ups, each timed with CUDA
+    events. Returns (TOPS, clock summary)."""
+    n = 8192
+    g = torch.Generator(device="cuda")
+    g.manual_seed(123)
+    a = torch.randint(-127, 128, (n, n), generator=g, device="cuda", dtype=torch.int8)
+    b = torch.randint(-127, 128, (n, n), generator=g, device="cuda", dtype=torch.int8)
+    for _ in range(3):
+        torch._int_mm(a, b)
+    best = float("inf")
+    with ClockSampler(gpu_index) as clocks:
+        for _ in range(10):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+    del a, b
+    return 2.0 * n ** 3 / (best * 1e-3) / 1e12, clocks.summary
 
 
 def w8a8_cpu_sample(x, w, layer, rows: int):
@@ -470,6 +510,7 @@ def run_double(args, rank, world):
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(local_rank) as clocks:
             torch.cuda.synchronize()
+            preroll(torch)
             start.record()
             for i in range(K):
                 fn(i, recs[i])
@@ -498,7 +539,7 @@ def run_double(args, rank, world):
         fb.qk_prep_into(di, c, e, fb.Freqs(dc[NUM_TXT:], dsn[NUM_TXT:], fr0.q_gain), H, qkv_j, NUM_TXT)
         return fb.attend_merged(*qkv_j)
 
-    e2e_steps = args.e2e_steps or max(3, K // 10)
+    e2e_steps = args.e2e_steps or max(E2E_MIN_STEPS, K // 10)
     pipe.run(2, e2e_compute)
     e2e_ms = pipe.run(e2e_steps, e2e_compute)
     pk, pk_kind = peaks()
@@ -530,10 +571,9 @@ def run_double(args, rank, world):
         "gpu_launches": 3 * K, "clocks": f["clocks"], "device_status": status,
     }
     if world == 1 and not args.no_cpu_baseline:
-        times, fl, threads, _ = cpu_sample(args.config, args.cpu_heads, reps=1)
-        line["cpu_baseline"] = {
-            "value": fl / times[0] / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"{args.cpu_heads} of {H} heads, batch 1, S={s}: plain-XLA path restated in torch fp32"}
+        m = cpu_measure(args.config)
+        line["cpu_baseline"] = {"value": m["value"], "unit": "TFLOP/s", "cores": m["cores"], "kind": "port",
+                                "sample": m["sample"]}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -605,6 +645,7 @@ def run_projection(args, rank, world):
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with ClockSampler(local_rank) as clocks:
             torch.cuda.synchronize()
+            preroll(torch)
             start.record()
             for i in range(K_steps):
                 fn(i, recs[i])
@@ -625,7 +666,7 @@ def run_projection(args, rank, world):
         projection.qkv_projection(dx, wt, dqs, dks, fb.Freqs(dc, dsn, fr0.q_gain), H, out=(o[0], o[1], o[2]))
         return o
 
-    e2e_steps = args.e2e_steps or max(3, K_steps // 10)
+    e2e_steps = args.e2e_steps or max(E2E_MIN_STEPS, K_steps // 10)
     pipe.run(2, e2e_compute)
     e2e_ms = pipe.run(e2e_steps, e2e_compute)
     pk, pk_kind = peaks()
@@ -654,6 +695,181 @@ def run_projection(args, rank, world):
 
 
 # ------------------------------------------------------------------ our arm
+def preroll(torch):
+    """Keep the GPU busy for ~5 ms (a spin kernel of torch's) before a timed region starts, so the
+    host enqueues the first steps while it spins: with the queue ahead of the GPU, the events
+    between kernels measure the kernels, not the host's per-call time."""
+    torch.cuda._sleep(10_000_000)
+
+
+def max_over_ranks(torch, dist, value, dev, world):
+    if world == 1:
+        return value
+    t = torch.tensor([value], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def measure_attention(args, torch, dist, fb, sharding, world, rank, dev, group, shard, gather, with_extras):
+    """Time K steps of qk_prep -> attend under one sharding; returns the fields of the JSON line.
+
+    shard "batch": rank r runs batch element r (seed r); "heads": one batch-1 call split by heads,
+    gathered by the attention epilogue's peer stores (gather "peer") or an NCCL all-gather.
+    `with_extras` adds the CUDA-graph replay (--graph) and the end-to-end leg.
+    """
+    from flicker_b200 import _lib
+
+    local_rank = dev.index
+    heads_total = NUM_HEADS
+    if shard == "heads" and world > 1:
+        h0, h1 = sharding.head_range(heads_total, world, rank)
+    else:
+        h0, h1 = 0, heads_total
+    heads_local = h1 - h0
+    seed = rank if (shard == "batch" and world > 1) else 0
+
+    sets = []
+    for i in range(2):  # two input sets, alternated, so no step finds its qkv in L2
+        qkv, qs, ks, freqs = make_inputs(torch, args.config, 1, heads_total, seed + 100 * i, dev)
+        if heads_local != heads_total:
+            qkv = sharding.slice_qkv_heads(qkv, heads_total, h0, h1)
+        sets.append((qkv.contiguous(), qs, ks, freqs))
+    s = sets[0][0].shape[1]
+    flops_local = attend_flops(1, s, heads_local)
+    bytes_local = qk_prep_bytes(1, s, heads_local)
+    split = _lib.lib().flk_attend_workspace_size(1, heads_local, s, HEAD_DIM) > 0
+
+    gathered = None
+    peer = None
+    if shard == "heads" and world > 1:
+        if gather == "peer":
+            peer = sharding.PeerOutput((1, s, heads_total * HEAD_DIM), dev, group)
+        else:
+            gathered = torch.empty((world, 1, heads_local, s, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+
+    def step(i, rec=None):
+        qkv, qs, ks, freqs = sets[i % 2]
+        if rec is not None:
+            rec[0].record()
+        q, k, v = fb.qk_prep(qkv, qs, ks, freqs, heads_local)
+        if rec is not None:
+            rec[1].record()
+        if peer is not None:
+            o = sharding.attend_gather_heads(q, k, v, peer, h0, heads_total, sync=False)
+        else:
+            o = fb.attend(q, k, v)
+        if rec is not None:
+            rec[2].record()
+        if peer is not None:
+            peer.barrier()
+        if gathered is not None:
+            sharding.gather_heads(o, gathered, group)
+        if rec is not None:
+            rec[3].record()
+        return o
+
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize()
+    if fb.device_status() != 0:
+        raise RuntimeError("device status reports a timed-out wait during warm-up")
+
+    K = args.steps
+    recs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(K)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        preroll(torch)
+        start.record()
+        for i in range(K):
+            step(i, recs[i])
+        end.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    elapsed_ms = max_over_ranks(torch, dist, start.elapsed_time(end), dev, world)
+    qk_all = [r[0].elapsed_time(r[1]) for r in recs]
+    at_all = [r[1].elapsed_time(r[2]) for r in recs]
+    ex_all = [r[2].elapsed_time(r[3]) for r in recs]
+    qk_ms, at_ms, ex_ms = statistics.mean(qk_all), statistics.mean(at_all), statistics.mean(ex_all)
+    status = fb.device_status()
+
+    # ---- optional: the same step replayed from CUDA graphs (one per input set), without the
+    # API's per-call host cost; the eager calls above are the headline
+    graph_line = None
+    if with_extras and args.graph and peer is None and gathered is None:
+        graphs = []
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for i in range(2):
+                step(i)
+        torch.cuda.current_stream().wait_stream(side)
+        for i in range(2):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                step(i)
+            graphs.append(gr)
+        for i in range(max(3, args.warmup)):
+            graphs[i % 2].replay()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        preroll(torch)
+        g0.record()
+        for i in range(K):
+            graphs[i % 2].replay()
+        g1.record()
+        torch.cuda.synchronize()
+        graph_ms = max_over_ranks(torch, dist, g0.elapsed_time(g1), dev, world)
+        graph_line = {"ms_per_step": graph_ms / K, "launches_per_step": 3 if split else 2}
+        del graphs
+        status = status or fb.device_status()
+
+    total_flops = flops_local * world if (shard == "batch" or world == 1) else attend_flops(1, s, heads_total)
+    out = {
+        "s": s, "heads_local": heads_local, "K": K, "elapsed_ms": elapsed_ms, "qk_all": qk_all, "at_all": at_all,
+        "qk_ms": qk_ms, "at_ms": at_ms, "ex_ms": ex_ms, "flops_local": flops_local, "bytes_local": bytes_local,
+        "total_flops": total_flops, "split": split, "status": status, "clocks": clocks.summary,
+        "graph": graph_line, "peer": peer is not None, "gathered": gathered is not None,
+    }
+    if not with_extras:
+        return out
+
+    # ---- end-to-end leg: host buffers through the public API, copies inside the timed region
+    e2e_steps = args.e2e_steps or max(E2E_MIN_STEPS, K // 10)
+    qkv0, qs0, ks0, freqs0 = sets[0]
+    host_in = [t.cpu().pin_memory() for t in (qkv0, freqs0.cos, freqs0.sin, qs0, ks0)]
+    if peer is not None:
+        out_shape = (1, s, heads_total * HEAD_DIM)
+    else:
+        out_shape = (1, heads_total if gathered is not None else heads_local, s, HEAD_DIM)
+    pipe = CopyPipeline(torch, host_in, out_shape, torch.bfloat16)
+
+    def e2e_compute(d):
+        d_qkv, d_cos, d_sin, d_qs, d_ks = d
+        q, k, v = fb.qk_prep(d_qkv, d_qs, d_ks, fb.Freqs(d_cos, d_sin, freqs0.q_gain), heads_local)
+        if peer is not None:
+            return sharding.attend_gather_heads(q, k, v, peer, h0, heads_total)
+        o = fb.attend(q, k, v)
+        if gathered is not None:
+            sharding.gather_heads(o, gathered, group)
+            return gathered.view(out_shape)
+        return o
+
+    persistent = peer is not None or gathered is not None
+    pipe.run(2, e2e_compute, persistent_out=persistent)
+    e2e_ms = pipe.run(e2e_steps, e2e_compute, before=(lambda: dist.barrier()) if world > 1 else None,
+                      persistent_out=persistent) * e2e_steps
+    out["e2e_ms"] = max_over_ranks(torch, dist, e2e_ms, dev, world)
+    out["e2e_steps"] = e2e_steps
+    out["h2d"], out["d2h"] = pipe.h2d_bytes, pipe.d2h_bytes
+    return out
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -682,184 +898,51 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     group = dist.group.WORLD if world > 1 else None
 
-    heads_total = NUM_HEADS
-    if args.shard == "heads" and world > 1:
-        h0, h1 = sharding.head_range(heads_total, world, rank)
-    else:
-        h0, h1 = 0, heads_total
-    heads_local = h1 - h0
-    seed = rank if (args.shard == "batch" and world > 1) else 0
-
-    sets = []
-    for i in range(2):  # two input sets, alternated, so no step finds its qkv in L2
-        qkv, qs, ks, freqs = make_inputs(torch, args.config, 1, heads_total, seed + 100 * i, dev)
-        if heads_local != heads_total:
-            qkv = sharding.slice_qkv_heads(qkv, heads_total, h0, h1)
-        sets.append((qkv.contiguous(), qs, ks, freqs))
-    s = sets[0][0].shape[1]
-    flops_local = attend_flops(1, s, heads_local)
-    bytes_local = qk_prep_bytes(1, s, heads_local)
-
-    gathered = None
-    peer = None
-    if args.shard == "heads" and world > 1:
-        if args.gather == "peer":
-            peer = sharding.PeerOutput((1, s, heads_total * HEAD_DIM), dev, group)
-        else:
-            gathered = torch.empty((world, 1, heads_local, s, HEAD_DIM), dtype=torch.bfloat16, device=dev)
-
-    def step(i, rec=None):
-        qkv, qs, ks, freqs = sets[i % 2]
-        if rec is not None:
-            rec[0].record()
-        q, k, v = fb.qk_prep(qkv, qs, ks, freqs, heads_local)
-        if rec is not None:
-            rec[1].record()
-        if peer is not None:
-            o = sharding.attend_gather_heads(q, k, v, peer, h0, heads_total)
-        else:
-            o = fb.attend(q, k, v)
-        if rec is not None:
-            rec[2].record()
-        if gathered is not None:
-            sharding.gather_heads(o, gathered, group)
-        return o
-
-    for i in range(max(3, args.warmup)):
-        step(i)
-    torch.cuda.synchronize()
-    if fb.device_status() != 0:
-        raise RuntimeError("device status reports a timed-out wait during warm-up")
-
-    K = args.steps
-    recs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local_rank) as clocks:
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        start.record()
-        for i in range(K):
-            step(i, recs[i])
-        end.record()
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-    elapsed_ms = start.elapsed_time(end)
-    qk_all = [r[0].elapsed_time(r[1]) for r in recs]
-    at_all = [r[1].elapsed_time(r[2]) for r in recs]
-    qk_ms, at_ms = statistics.mean(qk_all), statistics.mean(at_all)
-    if world > 1:
-        t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
-    status = fb.device_status()
-
-    # ---- optional: the same step replayed from CUDA graphs (one per input set), without the
-    # API's per-call host cost; the eager calls above are the headline
-    graph_line = None
-    if args.graph and peer is None and gathered is None:
-        graphs = []
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            for i in range(2):
-                step(i)
-        torch.cuda.current_stream().wait_stream(side)
-        for i in range(2):
-            gr = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(gr):
-                step(i)
-            graphs.append(gr)
-        for i in range(max(3, args.warmup)):
-            graphs[i % 2].replay()
-        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-        g0.record()
-        for i in range(K):
-            graphs[i % 2].replay()
-        g1.record()
-        torch.cuda.synchronize()
-        graph_ms = g0.elapsed_time(g1)
-        if world > 1:
-            t = torch.tensor([graph_ms], device=dev, dtype=torch.float64)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            graph_ms = float(t.item())
-        graph_line = {"ms_per_step": graph_ms / K, "launches_per_step": 2}
-        del graphs
-        status = status or fb.device_status()
-
-    # ---- end-to-end leg: host buffers through the public API, copies inside the timed region
-    e2e_steps = args.e2e_steps or max(3, K // 10)
-    qkv0, qs0, ks0, freqs0 = sets[0]
-    host_in = [t.cpu().pin_memory() for t in (qkv0, freqs0.cos, freqs0.sin, qs0, ks0)]
-    if peer is not None:
-        out_shape = (1, s, heads_total * HEAD_DIM)
-    else:
-        out_shape = (1, heads_total if gathered is not None else heads_local, s, HEAD_DIM)
-    pipe = CopyPipeline(torch, host_in, out_shape, torch.bfloat16)
-
-    def e2e_compute(d):
-        d_qkv, d_cos, d_sin, d_qs, d_ks = d
-        q, k, v = fb.qk_prep(d_qkv, d_qs, d_ks, fb.Freqs(d_cos, d_sin, freqs0.q_gain), heads_local)
-        if peer is not None:
-            return sharding.attend_gather_heads(q, k, v, peer, h0, heads_total)
-        o = fb.attend(q, k, v)
-        if gathered is not None:
-            sharding.gather_heads(o, gathered, group)
-            return gathered.view(out_shape)
-        return o
-
-    persistent = peer is not None or gathered is not None
-    pipe.run(2, e2e_compute, persistent_out=persistent)
-    e2e_ms = pipe.run(e2e_steps, e2e_compute, before=(lambda: dist.barrier()) if world > 1 else None,
-                      persistent_out=persistent) * e2e_steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
-    h2d, d2h = pipe.h2d_bytes, pipe.d2h_bytes
+    m = measure_attention(args, torch, dist, fb, sharding, world, rank, dev, group, args.shard, args.gather,
+                          with_extras=True)
+    # N > 1: the batch-1 call split by heads (strong scaling, the path with a real exchange), timed
+    # the same way in the same run and reported beside the batch-sharded headline
+    hs = None
+    if world > 1 and args.shard == "batch" and not args.no_heads_sharded:
+        hs = measure_attention(args, torch, dist, fb, sharding, world, rank, dev, group, "heads", args.gather,
+                               with_extras=False)
 
     pk, pk_kind = peaks()
+    s, heads_local, K = m["s"], m["heads_local"], m["K"]
+    at_tflops = m["flops_local"] / (m["at_ms"] * 1e-3) / 1e12
+    qk_gbs = m["bytes_local"] / (m["qk_ms"] * 1e-3) / 1e9
 
     def traffic(kernel):
         # captured at the single-GPU 1024^2 call with all 24 heads only
         return NCU_TRAFFIC_BYTES.get(f"{kernel}@{args.config}") if heads_local == NUM_HEADS else None
 
-    total_flops = flops_local * world if (args.shard == "batch" or world == 1) else attend_flops(1, s, heads_total)
-    value = total_flops * K / (elapsed_ms * 1e-3) / 1e12
-    e2e_value = total_flops * e2e_steps / (e2e_ms * 1e-3) / 1e12
-    at_tflops = flops_local / (at_ms * 1e-3) / 1e12
-    qk_gbs = bytes_local / (qk_ms * 1e-3) / 1e9
-
     line = None
     if rank == 0:
+        value = m["total_flops"] * K / (m["elapsed_ms"] * 1e-3) / 1e12
         line = {
             "metric": metric_for(args.config), "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": K,
-            "warmup": max(3, args.warmup), "ms_per_step": elapsed_ms / K, "higher_is_better": True,
+            "warmup": max(3, args.warmup), "ms_per_step": m["elapsed_ms"] / K, "higher_is_better": True,
             "scaling": "weak" if (args.shard == "batch" or world == 1) else "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {
                 "workload": f"flicker {args.config}^2 attention call: qk_prep + attend",
                 "batch": world if (args.shard == "batch" and world > 1) else 1,
-                "seq_len": s, "heads": heads_total, "head_dim": HEAD_DIM,
+                "seq_len": s, "heads": NUM_HEADS, "head_dim": HEAD_DIM,
                 "parallelism": (f"batch{world}" if args.shard == "batch" else
-                                (f"heads{world}+peer-store gather (merged heads)" if peer is not None
+                                (f"heads{world}+peer-store gather (merged heads)" if m["peer"]
                                  else f"heads{world}+nccl allgather"))
                 if world > 1 else "single",
                 "l2": "2 alternating input sets; per-step footprint (qkv + q,k,v + o) > 126 MB L2",
+                "timing": "device events; a ~5 ms spin kernel before the timed region lets the host run ahead",
             },
             "kernels": {
-                "qk_prep": {"us": qk_ms * 1e3, "us_p50": statistics.median(qk_all) * 1e3, "GB/s": qk_gbs,
-                            "bytes": bytes_local,
-                            "frac_hbm": qk_gbs / pk["hbm_gbs"]},
-                "attend": {"us": at_ms * 1e3, "us_p50": statistics.median(at_all) * 1e3, "TFLOP/s": at_tflops,
-                           "flops": flops_local,
+                "qk_prep": {"us": m["qk_ms"] * 1e3, "us_p50": statistics.median(m["qk_all"]) * 1e3, "GB/s": qk_gbs,
+                            "bytes": m["bytes_local"], "frac_hbm": qk_gbs / pk["hbm_gbs"]},
+                "attend": {"us": m["at_ms"] * 1e3, "us_p50": statistics.median(m["at_all"]) * 1e3,
+                           "TFLOP/s": at_tflops, "flops": m["flops_local"],
                            # exponentials: B*H*S^2 per call; 3 of 4 on MUFU.EX2 (16 per clock per SM),
                            # 1 of 4 on the FMA-pipe polynomial
-                           "exp": exp_check(s, heads_local, at_ms, clocks.summary),
+                           "exp": exp_check(s, heads_local, m["at_ms"], m["clocks"]),
                            "frac_bf16": at_tflops / pk["bf16_tflops"],
                            # the same against cuBLAS held for seconds under the 1 kW cap: the timed
                            # loop runs long enough for the cap to act (later rounds run slower)
@@ -868,33 +951,68 @@ def main():
             },
             "roofline": {"bound": "tensor", "achieved": at_tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": at_tflops / pk["bf16_tflops"], "traffic": traffic("attend"),
+                         "traffic_source": NCU_TRAFFIC_NOTE,
                          "peak_source": f"{pk_kind} bf16 burst (cuBLAS)", "kernel": "attend"},
             "roofline_qk_prep": {"bound": "hbm", "achieved": qk_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                                  "frac": qk_gbs / pk["hbm_gbs"], "traffic": traffic("qk_prep"),
-                                 "peak_source": f"{pk_kind} HBM copy"},
-            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "steps": e2e_steps, "ms_per_step": e2e_ms / e2e_steps},
-            "gpu_launches": 2 * K,
-            "clocks": clocks.summary,
-            "device_status": status,
+                                 "traffic_source": NCU_TRAFFIC_NOTE, "peak_source": f"{pk_kind} HBM copy"},
+            "e2e": {"value": m["total_flops"] * m["e2e_steps"] / (m["e2e_ms"] * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": m["h2d"], "d2h_bytes_per_step": m["d2h"],
+                    "steps": m["e2e_steps"], "ms_per_step": m["e2e_ms"] / m["e2e_steps"]},
+            "gpu_launches": (3 if m["split"] else 2) * K,
+            "clocks": m["clocks"],
+            "device_status": m["status"],
         }
-        if graph_line is not None:
-            graph_line["value"] = total_flops / (graph_line["ms_per_step"] * 1e-3) / 1e12
-            graph_line["unit"] = "TFLOP/s"
-            line["graph"] = graph_line
+        if m["graph"] is not None:
+            m["graph"]["value"] = m["total_flops"] / (m["graph"]["ms_per_step"] * 1e-3) / 1e12
+            m["graph"]["unit"] = "TFLOP/s"
+            line["graph"] = m["graph"]
+        if hs is not None:
+            hs_at = hs["flops_local"] / (hs["at_ms"] * 1e-3) / 1e12
+            hs_value = hs["total_flops"] * hs["K"] / (hs["elapsed_ms"] * 1e-3) / 1e12
+            line["heads_sharded"] = {
+                "workload": f"one batch-1 call split by heads: {hs['heads_local']} of {NUM_HEADS} heads per rank, "
+                            + ("gathered by the attention epilogue's stores into every rank's buffer"
+                               if hs["peer"] else "gathered by an NCCL all-gather"),
+                "scaling": "strong", "value": hs_value, "unit": "TFLOP/s",
+                "ms_per_step": hs["elapsed_ms"] / hs["K"],
+                "qk_prep_us": hs["qk_ms"] * 1e3, "attend_us": hs["at_ms"] * 1e3,
+                "gather_sync_us": hs["ex_ms"] * 1e3,
+                "attend_frac_bf16": hs_at / pk["bf16_tflops"],
+                "split_kv": hs["split"], "device_status": hs["status"], "clocks": hs["clocks"],
+                "note": "rank 0's kernel times; ms_per_step is the max over ranks",
+            }
+            line["gpu_launches"] += (3 if hs["split"] else 2) * hs["K"]
     if world > 1:
-        peer = None  # release the symmetric-memory buffers before the group goes away
+        import gc
+
+        m = hs = None
+        gc.collect()  # release the symmetric-memory buffers before the group goes away
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
-            times, fl, threads, _ = cpu_sample(args.config, args.cpu_heads, reps=1)
-            line["cpu_baseline"] = {
-                "value": fl / times[0] / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                "sample": f"{args.cpu_heads} of {NUM_HEADS} heads, batch 1, S={s}: plain-XLA path restated in "
-                          f"torch fp32 (heads, rms_norm, apply_rope, sdpa)"}
+            line["cpu_baseline"] = cpu_baseline_subprocess(args.config)
         print(json.dumps(line), flush=True)
     return 0
+
+
+def cpu_baseline_subprocess(config):
+    """The reference arm itself (`--impl reference`, its default 20 runs after 3 warm-ups), run in a
+    fresh process without a GPU, so the `cpu_baseline` leg and the reference arm are one
+    measurement method under the same conditions (no CUDA context, a fresh allocator)."""
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    for key in ("RANK", "WORLD_SIZE", "LOCAL_RANK"):
+        env.pop(key, None)
+    proc = subprocess.run([sys.executable, os.path.abspath(__file__), "--impl", "reference", "--config", config,
+                           "--steps", str(CPU_RUNS), "--warmup", str(CPU_WARMUP)], env=env, capture_output=True,
+                          text=True, timeout=900)
+    lines = [ln for ln in proc.stdout.splitlines() if ln.startswith("{")]
+    if proc.returncode != 0 or not lines:
+        return {"value": None, "unit": "TFLOP/s", "kind": "port", "cores": os.cpu_count(),
+                "sample": f"reference arm failed: {proc.stderr.strip()[-300:]}"}
+    ref = json.loads(lines[-1])
+    return dict(ref["cpu_baseline"])
 
 
 if __name__ == "__main__":

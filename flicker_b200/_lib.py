@@ -53,6 +53,9 @@ SIGNATURES = {
     "flk_selftest_wait_timeout": (_int, [ctypes.c_void_p, ctypes.c_void_p]),
     "flk_selftest_quotient": (_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p,
                                      ctypes.c_void_p, ctypes.c_void_p]),
+    "flk_selftest_exp2": (_int, [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p, ctypes.c_void_p,
+                                 ctypes.c_void_p]),
+    "flk_kernel_binary_version": (_int, []),
     "flk_error_string": (ctypes.c_char_p, [_int]),
     "flk_abi_version": (_int, []),
 }

@@ -37,6 +37,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <mutex>
 
 #include "flicker_b200.h"
 #include "ptx.cuh"
@@ -877,18 +878,27 @@ int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
                       const OutLayout& out, int splits, void* workspace, int* status, cudaStream_t stream) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return FLK_ERR_CUDA;
+  if (dev < 0 || dev >= 64) return FLK_ERR_UNSUPPORTED;
+  // Per-device set-up on first use, under a lock: host threads making their first call on the
+  // same device at the same time must not see the SM count before it is set.
+  static std::mutex setup_mu;
   static bool configured[64] = {};
   static int sm_count[64] = {};
-  if (dev < 0 || dev >= 64) return FLK_ERR_UNSUPPORTED;
-  if (!configured[dev]) {
-    if (cudaFuncSetAttribute(attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(attend_smem_bytes())) != cudaSuccess ||
-        cudaFuncSetAttribute(attend_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(attend_smem_bytes())) != cudaSuccess ||
-        cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
-        sm_count[dev] <= 0)
-      return FLK_ERR_CUDA;
-    configured[dev] = true;
+  int sms = 0;
+  {
+    std::lock_guard<std::mutex> lock(setup_mu);
+    if (!configured[dev]) {
+      int n = 0;
+      if (cudaFuncSetAttribute(attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(attend_smem_bytes())) != cudaSuccess ||
+          cudaFuncSetAttribute(attend_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(attend_smem_bytes())) != cudaSuccess ||
+          cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+        return FLK_ERR_CUDA;
+      sm_count[dev] = n;
+      configured[dev] = true;
+    }
+    sms = sm_count[dev];
   }
   const long long rows = static_cast<long long>(B) * H * S;
   CUtensorMap mq, mk, mv;
@@ -916,7 +926,7 @@ int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
   // TMA-staged epilogue, which borrows the Q buffers.
   const bool persistent = !p.tma_out;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = persistent ? dim3(static_cast<unsigned>(std::min<long long>(items, sm_count[dev])))
+  cfg.gridDim = persistent ? dim3(static_cast<unsigned>(std::min<long long>(items, sms)))
                            : dim3(p.n_pairs, p.BH, splits);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = attend_smem_bytes();
@@ -965,6 +975,13 @@ int launch_attend_gather(const uint16_t* q, const uint16_t* k, const uint16_t* v
   out.n_out = n_out;
   for (int d = 0; d < n_out; ++d) out.o[d] = outs[d];
   return launch_attend_out(q, k, v, B, H, S, out, splits, workspace, status, stream);
+}
+
+int attend_binary_version(int* version) {
+  cudaFuncAttributes a{};
+  if (cudaFuncGetAttributes(&a, attend_persistent_kernel) != cudaSuccess) return FLK_ERR_CUDA;
+  *version = a.binaryVersion;
+  return FLK_OK;
 }
 
 // Head-major output ([B, H, S, 128]), the layout of kernels.attend.

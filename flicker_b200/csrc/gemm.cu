@@ -32,6 +32,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <mutex>
 
 #include "flicker_b200.h"
 #include "ptx.cuh"
@@ -495,13 +496,17 @@ template <GemmKind KD, GemmEpi EP>
 int launch_pair(const void* x, const void* wt, PairParams p, int sms, cudaStream_t stream) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FLK_ERR_CUDA;
+  static std::mutex setup_mu;  // first calls from several host threads set up once
   static bool configured[64] = {};
   const size_t smem = sizeof(PairSmem) + 1024;
-  if (!configured[dev]) {
-    if (cudaFuncSetAttribute(gemm_pair_kernel<KD, EP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
-      return FLK_ERR_CUDA;
-    configured[dev] = true;
+  {
+    std::lock_guard<std::mutex> lock(setup_mu);
+    if (!configured[dev]) {
+      if (cudaFuncSetAttribute(gemm_pair_kernel<KD, EP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(smem)) != cudaSuccess)
+        return FLK_ERR_CUDA;
+      configured[dev] = true;
+    }
   }
   CUtensorMap ma, mb;
   if (!make_operand_map<KD>(&ma, x, p.M, p.K) || !make_operand_map<KD>(&mb, wt, p.N, p.K)) return FLK_ERR_CUDA;

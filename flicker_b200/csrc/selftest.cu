@@ -44,7 +44,27 @@ __global__ void __launch_bounds__(256) quotient_kernel(const float* a, const flo
   q_ref[i] = __fdiv_rn(x, y);
 }
 
+// The two ways attend computes 2^x for p = exp(s) (x = s * log2(e)), element by element:
+// poly[i] = exp2_poly2 (FMA pipe, degree-4 minimax polynomial), mufu[i] = ex2.approx (SFU).
+__global__ void __launch_bounds__(256) exp2_kernel(const float* x, long long n, float* poly, float* mufu) {
+  const long long i = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 2;
+  if (i >= n) return;
+  const bool pair = i + 1 < n;
+  const float2 v = make_float2(x[i], pair ? x[i + 1] : 0.0f);
+  const float2 e = exp2_poly2(v);
+  poly[i] = e.x;
+  mufu[i] = ex2_approx(v.x);
+  if (pair) {
+    poly[i + 1] = e.y;
+    mufu[i + 1] = ex2_approx(v.y);
+  }
+}
+
 }  // namespace
+
+// binaryVersion (major * 10 + minor) of the code the runtime loaded for the attention kernel.
+int attend_binary_version(int* version);
+
 }  // namespace flk
 
 extern "C" int flk_selftest_wait_timeout(int* result, void* stream) {
@@ -66,4 +86,23 @@ extern "C" int flk_selftest_quotient(const float* a, const float* b, long long n
   flk::quotient_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       a, b, n, q_fast, q_ref);
   return cudaGetLastError() == cudaSuccess ? FLK_OK : FLK_ERR_CUDA;
+}
+
+// flk_selftest_exp2: the attend kernel's two exponentials (polynomial and MUFU.EX2) for n device
+// floats, so a test can bound their relative error against a float64 reference.
+extern "C" int flk_selftest_exp2(const float* x, long long n, float* poly, float* mufu, void* stream) {
+  if (n < 0 || (n > 0 && (x == nullptr || poly == nullptr || mufu == nullptr))) return FLK_ERR_INVALID_ARGUMENT;
+  if (n == 0) return FLK_OK;
+  const long long threads = (n + 1) / 2;
+  flk::exp2_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, n, poly, mufu);
+  return cudaGetLastError() == cudaSuccess ? FLK_OK : FLK_ERR_CUDA;
+}
+
+// flk_kernel_binary_version: which code the runtime loaded for this library's kernels on the
+// current device (100 = sm_100), read from the attention kernel's attributes.
+extern "C" int flk_kernel_binary_version(void) {
+  int version = 0;
+  const int rc = flk::attend_binary_version(&version);
+  return rc == FLK_OK ? version : rc;
 }

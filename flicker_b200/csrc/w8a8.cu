@@ -23,6 +23,7 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <mutex>
 
 #include "flicker_b200.h"
 #include "ptx.cuh"
@@ -422,13 +423,17 @@ static int launch_w8a8_gemm_single(const CUtensorMap& ma, const CUtensorMap& mb,
                                    cudaStream_t stream) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return FLK_ERR_CUDA;
+  static std::mutex setup_mu;  // first calls from several host threads set up once
   static bool configured[64] = {};
   const size_t smem = sizeof(GemmSmem) + 1024;
-  if (!configured[dev]) {
-    if (cudaFuncSetAttribute(w8a8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
-      return FLK_ERR_CUDA;
-    configured[dev] = true;
+  {
+    std::lock_guard<std::mutex> lock(setup_mu);
+    if (!configured[dev]) {
+      if (cudaFuncSetAttribute(w8a8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(smem)) != cudaSuccess)
+        return FLK_ERR_CUDA;
+      configured[dev] = true;
+    }
   }
   const int grid = std::min(p.n_tiles, sms);
   w8a8_gemm_kernel<<<grid, kGemmThreads, smem, stream>>>(ma, mb, p);

@@ -92,13 +92,21 @@ class PeerOutput:
             self.handles.append(handle)
             self.ptrs.append([int(p) for p in handle.buffer_ptrs])
         self.turn = 0
+        self.last = 0  # buffer of the most recent call
+
+    def barrier(self) -> None:
+        """The barrier that ends a call made with ``sync=False``: after it, every rank's stores
+        into the most recently used buffer are complete and visible."""
+        self.handles[self.last].barrier()
 
 
 def attend_gather_heads(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, peer: PeerOutput, h0: int,
-                        num_heads: int) -> torch.Tensor:
+                        num_heads: int, sync: bool = True) -> torch.Tensor:
     """Head-sharded attention whose epilogue stores this rank's heads [h0, h0 + H) of the merged
     rows into every rank's buffer; after the barrier, the returned local buffer holds
-    merge_heads(attend(q, k, v)) over all ``num_heads`` heads on every rank."""
+    merge_heads(attend(q, k, v)) over all ``num_heads`` heads on every rank. ``sync=False`` leaves
+    the barrier to the caller (``peer.barrier()``), which must make it before using the buffer
+    and before the next call."""
     import ctypes
 
     from . import _lib, kernels
@@ -106,6 +114,7 @@ def attend_gather_heads(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, peer:
     q, k, v, batch, heads, length, dim = kernels._attend_args(q, k, v, None)
     i = peer.turn
     peer.turn = (peer.turn + 1) % len(peer.bufs)
+    peer.last = i
     buf, handle, ptrs = peer.bufs[i], peer.handles[i], peer.ptrs[i]
     if tuple(buf.shape) != (batch, length, num_heads * dim):
         raise ValueError(f"peer buffer {tuple(buf.shape)} is not [B, S, H*D] = {(batch, length, num_heads * dim)}")
@@ -118,5 +127,6 @@ def attend_gather_heads(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, peer:
                                      len(ptrs), num_heads, h0, ws.data_ptr() if ws is not None else None,
                                      ws_bytes, kernels._stream(q))
     _lib.check("flk_attend_gather", code)
-    handle.barrier()
+    if sync:
+        handle.barrier()
     return buf

@@ -108,12 +108,15 @@ size_t flk_attend_workspace_size(int B, int H, int S, int D);
 
 /*
  * flk_attend for callers that cannot allocate device memory. No counterpart in the reference.
- * Same arguments and result as flk_attend minus the workspace: when the shape runs split over
- * KV, the partial results go to a 16 MiB scratch array built into the library (held on every
- * GPU that loads it) instead of caller memory, so the call allocates nothing. Shapes needing
- * more than 16 MiB of split scratch return FLK_ERR_WORKSPACE. The first call on a device sets
- * up the scratch address (make it before any stream capture); calls share the scratch, so
- * calls whose kernels overlap on the GPU race and must be ordered by the caller.
+ * Same arguments as flk_attend minus the workspace, and the same result as flk_attend given the
+ * workspace it asks for: when the shape runs split over KV, the partial results go to a 16 MiB
+ * scratch array built into the library (held on every GPU that loads it) instead of caller
+ * memory, so the call allocates nothing. Shapes whose split needs more than 16 MiB of scratch
+ * (e.g. B=1, H=2, S=8192 on a 148-SM B200) return FLK_ERR_WORKSPACE, although flk_attend with
+ * no workspace (NULL, 0) runs them unsplit: this entry point never silently changes the split.
+ * The first call on a device sets up the scratch address (make it before any stream capture);
+ * calls share the scratch, so calls whose kernels overlap on the GPU race and must be ordered
+ * by the caller.
  */
 int flk_attend_noalloc(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                        int B, int H, int S, int D, uint16_t* o, void* stream);
@@ -183,6 +186,16 @@ int flk_selftest_wait_timeout(int* result, void* stream);
  * Markstein's FMA correction per element): writes that quotient and __fdiv_rn's for n pairs of
  * device floats (a[i] / b[i]) into q_fast and q_ref. No reference counterpart (device check). */
 int flk_selftest_quotient(const float* a, const float* b, long long n, float* q_fast, float* q_ref, void* stream);
+
+/* Self-test of the attend kernel's exponentials (no reference counterpart; device check): for n
+ * device floats x, poly[i] = 2^x[i] from the FMA-pipe polynomial that computes one exponential in
+ * four of kernels.attend's p = exp(s) (src/flicker/kernels.py:124), mufu[i] = 2^x[i] from
+ * ex2.approx (the other three). A test bounds both against float64 over the bounded-logit domain. */
+int flk_selftest_exp2(const float* x, long long n, float* poly, float* mufu, void* stream);
+
+/* binaryVersion (major * 10 + minor, 100 = sm_100) of the code the CUDA runtime loaded for this
+ * library's kernels on the current device, or a negative FLK_ERR_* code. No reference counterpart. */
+int flk_kernel_binary_version(void);
 
 /* Reads (and clears) the device-side status word of the current device: 0 or FLK_ERR_DEVICE_TIMEOUT.
  * Synchronises the device. */

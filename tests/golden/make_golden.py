@@ -109,9 +109,11 @@ def bound_cases(ref):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-src", default=os.environ.get("FLICKER_REFERENCE_SRC",
-                                                              "/root/reference/src"))
+    ap.add_argument("--reference-src", default=os.environ.get("FLICKER_REFERENCE_SRC"),
+                    help="the reference checkout's src/ directory (or set FLICKER_REFERENCE_SRC)")
     args = ap.parse_args()
+    if not args.reference_src:
+        ap.error("pass --reference-src or set FLICKER_REFERENCE_SRC to the reference's src/ directory")
     sys.path.insert(0, HERE)
     import jax_stand_in
 

@@ -38,7 +38,9 @@ def test_reference_arm_prints_one_contract_line():
     assert line["impl"] == "reference"
     assert line["metric"] == load_bench().metric_for("512")
     assert line["unit"] == "TFLOP/s" and line["higher_is_better"] is True
-    assert line["value"] > 0 and line["n_gpus"] == 1 and line["steps"] == 1 and line["warmup"] == 0
+    # the median of at least 20 timed runs after at least 3 warm-ups, whatever --steps/--warmup ask for
+    assert line["value"] > 0 and line["n_gpus"] == 1 and line["steps"] == 20 and line["warmup"] == 3
+    assert line["ms_per_step"] > 0 and "median of 20 runs" in line["cpu_baseline"]["sample"]
     assert line["config"]["seq_len"] == 1536 and line["config"]["heads"] == 24
     cpu = line["cpu_baseline"]
     assert cpu["kind"] == "port" and cpu["cores"] >= 1 and cpu["value"] == line["value"]

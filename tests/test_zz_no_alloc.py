@@ -74,7 +74,10 @@ def test_no_alloc_matches_workspace_entry_point_twice(b, h, s):
 
 def test_no_alloc_refuses_shapes_beyond_its_scratch():
     lib = _lib.lib()
-    # batch 1, 2 heads, S = 8192 runs split over KV and would need ~16.9 MB (> 16 MiB) of scratch.
+    # batch 1, 2 heads, S = 8192 runs split over KV on a 148-SM B200 and would need ~16.9 MB
+    # (> 16 MiB) of scratch. On a device with fewer SMs the shape may not split at all.
+    if lib.flk_attend_workspace_size(1, 2, 8192, 128) <= 16 << 20:
+        pytest.skip("this device runs the shape without a split over KV")
     q, k, v = qkv_inputs(1, 2, 8192, seed=3)
     o = torch.empty_like(q)
     code = lib.flk_attend_noalloc(q.data_ptr(), k.data_ptr(), v.data_ptr(), 1, 2, 8192, 128, o.data_ptr(), None)
