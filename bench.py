@@ -22,8 +22,13 @@ Multi-GPU (torchrun, one process per GPU, NCCL):
                  --gather peer (default): the attention epilogue stores each
                  rank's heads, merged ([1, S, 24*128]), straight into every
                  rank's output over NVLink (TMA stores into symmetric memory),
-                 then one barrier; --gather nccl: attend, then an NCCL
-                 all-gather of [1, 24/N, S, 128].
+                 then one barrier; --gather multicast: the same rows stored once
+                 through the output buffers' NVLink multicast address (multimem
+                 stores the NVSwitch replicates into every rank's buffer);
+                 --gather nccl: attend, then an NCCL all-gather of
+                 [1, 24/N, S, 128].
+  With --shard batch and N > 1 the line also carries `heads_sharded`: the batch-1
+  call split by heads, timed the same way in the same run.
 
 --impl reference times the reference's plain-XLA path restated on the host
 cores (jax is not installable, see oracle/cpu_baseline.py) on the same config.
@@ -77,8 +82,9 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(GRIDS), default="1024")
     ap.add_argument("--shard", choices=["batch", "heads"], default="batch")
-    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
-                    help="--shard heads: epilogue stores into every rank's buffer, or an NCCL all-gather")
+    ap.add_argument("--gather", choices=["peer", "multicast", "nccl"], default="peer",
+                    help="head sharding: epilogue stores into every rank's buffer or through the buffers' "
+                         "multicast address, or an NCCL all-gather")
     ap.add_argument("--e2e-steps", type=int, default=None,
                     help=f"steps of the end-to-end leg (default max({E2E_MIN_STEPS}, K/10))")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -742,10 +748,14 @@ def measure_attention(args, torch, dist, fb, sharding, world, rank, dev, group, 
     gathered = None
     peer = None
     if shard == "heads" and world > 1:
-        if gather == "peer":
+        if gather != "nccl":
             peer = sharding.PeerOutput((1, s, heads_total * HEAD_DIM), dev, group)
+            if gather == "multicast" and not peer.multicast:
+                raise RuntimeError("--gather multicast: this node has no NVLink multicast for these buffers")
         else:
             gathered = torch.empty((world, 1, heads_local, s, HEAD_DIM), dtype=torch.bfloat16, device=dev)
+
+    use_mc = peer is not None and gather == "multicast"
 
     def step(i, rec=None):
         qkv, qs, ks, freqs = sets[i % 2]
@@ -755,7 +765,7 @@ def measure_attention(args, torch, dist, fb, sharding, world, rank, dev, group, 
         if rec is not None:
             rec[1].record()
         if peer is not None:
-            o = sharding.attend_gather_heads(q, k, v, peer, h0, heads_total, sync=False)
+            o = sharding.attend_gather_heads(q, k, v, peer, h0, heads_total, sync=False, multicast=use_mc)
         else:
             o = fb.attend(q, k, v)
         if rec is not None:
@@ -834,7 +844,7 @@ def measure_attention(args, torch, dist, fb, sharding, world, rank, dev, group, 
         "s": s, "heads_local": heads_local, "K": K, "elapsed_ms": elapsed_ms, "qk_all": qk_all, "at_all": at_all,
         "qk_ms": qk_ms, "at_ms": at_ms, "ex_ms": ex_ms, "flops_local": flops_local, "bytes_local": bytes_local,
         "total_flops": total_flops, "split": split, "status": status, "clocks": clocks.summary,
-        "graph": graph_line, "peer": peer is not None, "gathered": gathered is not None,
+        "graph": graph_line, "peer": peer is not None, "gathered": gathered is not None, "multicast": use_mc,
     }
     if not with_extras:
         return out
@@ -853,7 +863,7 @@ def measure_attention(args, torch, dist, fb, sharding, world, rank, dev, group, 
         d_qkv, d_cos, d_sin, d_qs, d_ks = d
         q, k, v = fb.qk_prep(d_qkv, d_qs, d_ks, fb.Freqs(d_cos, d_sin, freqs0.q_gain), heads_local)
         if peer is not None:
-            return sharding.attend_gather_heads(q, k, v, peer, h0, heads_total)
+            return sharding.attend_gather_heads(q, k, v, peer, h0, heads_total, multicast=use_mc)
         o = fb.attend(q, k, v)
         if gathered is not None:
             sharding.gather_heads(o, gathered, group)
@@ -929,7 +939,8 @@ def main():
                 "batch": world if (args.shard == "batch" and world > 1) else 1,
                 "seq_len": s, "heads": NUM_HEADS, "head_dim": HEAD_DIM,
                 "parallelism": (f"batch{world}" if args.shard == "batch" else
-                                (f"heads{world}+peer-store gather (merged heads)" if m["peer"]
+                                (f"heads{world}+multicast-store gather (merged heads)" if m["multicast"]
+                                 else f"heads{world}+peer-store gather (merged heads)" if m["peer"]
                                  else f"heads{world}+nccl allgather"))
                 if world > 1 else "single",
                 "l2": "2 alternating input sets; per-step footprint (qkv + q,k,v + o) > 126 MB L2",
@@ -972,7 +983,9 @@ def main():
             hs_value = hs["total_flops"] * hs["K"] / (hs["elapsed_ms"] * 1e-3) / 1e12
             line["heads_sharded"] = {
                 "workload": f"one batch-1 call split by heads: {hs['heads_local']} of {NUM_HEADS} heads per rank, "
-                            + ("gathered by the attention epilogue's stores into every rank's buffer"
+                            + ("gathered by the attention epilogue's multimem stores through the output "
+                               "buffers' NVLink multicast address" if hs["multicast"] else
+                               "gathered by the attention epilogue's stores into every rank's buffer"
                                if hs["peer"] else "gathered by an NCCL all-gather"),
                 "scaling": "strong", "value": hs_value, "unit": "TFLOP/s",
                 "ms_per_step": hs["elapsed_ms"] / hs["K"],

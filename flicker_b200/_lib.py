@@ -34,6 +34,8 @@ SIGNATURES = {
                                  ctypes.c_size_t, ctypes.c_void_p]),
     "flk_attend_gather": (_int, [_u16p, _u16p, _u16p, _int, _int, _int, _int, ctypes.POINTER(ctypes.c_void_p),
                                  _int, _int, _int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "flk_attend_gather_multicast": (_int, [_u16p, _u16p, _u16p, _int, _int, _int, _int, _u16p, _int, _int,
+                                           ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "flk_linear": (_int, [_u16p, _u16p, _int, _int, _int, _u16p, ctypes.c_void_p]),
     "flk_linear_qk_prep": (_int, [_u16p, _u16p, _int, _int, _int, _u16p, _u16p, _f32p, _f32p, ctypes.c_float,
                                   _int, _int, _int, _int, _u16p, _u16p, _u16p, _int, _int, ctypes.c_void_p,

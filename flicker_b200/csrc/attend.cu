@@ -85,7 +85,10 @@ struct alignas(1024) Smem {
 // Where the bf16 output rows go. Head-major [B, H, S, 128] (kernels.attend), or heads merged into
 // [B, S, H_out * 128] rows (merge_heads) with this call's head h at position h0 + h, written
 // into each of the n_out buffers: one buffer normally; this GPU's and every peer's output when a
-// head-sharded call gathers its heads by storing them straight into the peers' memory.
+// head-sharded call gathers its heads by storing them straight into the peers' memory. With
+// `multicast`, o[0] is an NVLink multicast address bound to every rank's output buffer: each
+// 16-byte store is a multimem.st, which the NVSwitch replicates into all of them, so a row
+// leaves this GPU once however many ranks receive it.
 constexpr int kMaxOuts = 8;
 struct OutLayout {
   int merged;
@@ -93,8 +96,16 @@ struct OutLayout {
   int H_out;  // heads per merged output row
   int h0;     // first head of this call within a merged row
   int n_out;
+  int multicast;
   uint16_t* o[kMaxOuts];
 };
+
+// One 16-byte store through a multicast address (every GPU bound to it receives the bytes).
+__device__ __forceinline__ void multimem_st16(void* addr, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
 
 struct Params {
   int S;          // sequence length (multiple of 128)
@@ -108,6 +119,10 @@ struct Params {
   // outputs) and the CTA writes o itself: one TMA map per buffer over [B*S, H_out*128] bf16,
   // 64-column x 32-row boxes with the 128-byte swizzle, so each warp's block leaves as one tile.
   int tma_out;
+  // When a merged output goes through a multicast address and the CTA writes o itself: the
+  // 32 x 64 block of each softmax warp is staged in shared memory as for tma_out, then stored by
+  // multimem.st in whole 128-byte row pieces (8 lanes per row), which NVLink carries as full lines.
+  int stage_mc;
   CUtensorMap out_maps[kMaxOuts];
   float* acc;     // split > 1: [n_splits, B*H*S, 128] fp32 un-normalised partial P.V
   float* lsum;    // split > 1: [n_splits, B*H*S] fp32 partial row sums
@@ -198,6 +213,12 @@ __device__ __forceinline__ size_t out_row(size_t grow, int S, const OutLayout& L
 // system-scope fence, so that its stores are visible before whatever synchronisation the
 // caller performs after the kernel.
 __device__ __forceinline__ void store_out(const OutLayout& L, size_t off, const uint32_t (&pk)[16]) {
+  if (L.multicast) {
+    uint4* dst = reinterpret_cast<uint4*>(L.o[0] + off);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) multimem_st16(dst + i, make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]));
+    return;
+  }
 #pragma unroll 1
   for (int d = 0; d < L.n_out; ++d) {
     uint4* dst = reinterpret_cast<uint4*>(L.o[d] + off);
@@ -222,9 +243,10 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int c0, int
 __device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t grow, int half, int split, float l,
                                         uint8_t* stage) {
   const float rl = __frcp_rn(l);
-  if (p.n_splits == 1 && p.tma_out) {
+  if (p.n_splits == 1 && (p.tma_out || p.stage_mc)) {
     // Stage the 32 x 64 block in the 128-byte-swizzled layout the maps expect (16-byte unit j of
-    // row r at position j ^ (r & 7): conflict-free), then one lane stores it to every buffer.
+    // row r at position j ^ (r & 7): conflict-free), then one lane stores it to every buffer
+    // (tma_out) or the warp stores it through the multicast address (stage_mc).
     const int lane = threadIdx.x & 31;
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {
@@ -242,6 +264,20 @@ __device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t
         *reinterpret_cast<uint4*>(stage + lane * 128 + ((j ^ (lane & 7)) << 4)) =
             make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
       }
+    }
+    if (p.stage_mc) {
+      __syncwarp();
+      const size_t first = grow - lane;  // the block's first query row
+      const int u = lane & 7;
+#pragma unroll 1
+      for (int i = 0; i < 8; ++i) {
+        const int r = i * 4 + (lane >> 3);
+        const uint4 v = *reinterpret_cast<const uint4*>(stage + r * 128 + ((u ^ (r & 7)) << 4));
+        multimem_st16(p.out.o[0] + out_row(first + r, p.S, p.out) * kDim + half * 64 + u * 8, v);
+      }
+      __threadfence_system();
+      __syncwarp();
+      return;
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
@@ -271,7 +307,7 @@ __device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t
                             quotient_rn(__uint_as_float(r[2 * i + 1]), l, rl));
       store_out(p.out, orow + c * 32, pk);
     }
-    if (p.out.n_out > 1) __threadfence_system();
+    if (p.out.n_out > 1 || p.out.multicast) __threadfence_system();
   } else {
     // Partial result of this split: un-normalised fp32 accumulator and row sum.
     const size_t plane = static_cast<size_t>(p.BH) * p.S;  // rows per split
@@ -784,9 +820,13 @@ __global__ void __launch_bounds__(256) combine_splits_kernel(const float* __rest
 #pragma unroll
   for (int i = 0; i < 4; ++i) pk[i] = pack_bf16x2(quotient_rn(a[2 * i], l, rl), quotient_rn(a[2 * i + 1], l, rl));
   const size_t off = out_row(row, S, L) * kDim + col;
+  if (L.multicast) {
+    multimem_st16(L.o[0] + off, make_uint4(pk[0], pk[1], pk[2], pk[3]));
+  } else {
 #pragma unroll 1
-  for (int d = 0; d < L.n_out; ++d) *reinterpret_cast<uint4*>(L.o[d] + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-  if (L.n_out > 1) __threadfence_system();
+    for (int d = 0; d < L.n_out; ++d) *reinterpret_cast<uint4*>(L.o[d] + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  }
+  if (L.n_out > 1 || L.multicast) __threadfence_system();
 }
 
 }  // namespace
@@ -901,6 +941,12 @@ int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
     sms = sm_count[dev];
   }
   const long long rows = static_cast<long long>(B) * H * S;
+  // Gathering calls that write o themselves stage each warp's block in shared memory (the Q
+  // buffers, free once the item's UMMAs are done) and store it as whole rows: by TMA into every
+  // buffer, or by multimem stores through a multicast address.
+  const bool staged = out.merged && (out.n_out > 1 || out.multicast) && splits == 1;
+  const bool tma_out = staged && !out.multicast;
+  const bool persistent = !staged;
   CUtensorMap mq, mk, mv;
   if (!make_tile_map(&mq, q, rows) || !make_tile_map(&mk, k, rows) || !make_tile_map(&mv, v, rows))
     return FLK_ERR_CUDA;
@@ -914,7 +960,8 @@ int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
   if (items > INT32_MAX) return FLK_ERR_UNSUPPORTED;
   p.n_items = static_cast<int>(items);
   p.out = out;
-  p.tma_out = (out.merged && out.n_out > 1 && splits == 1) ? 1 : 0;
+  p.tma_out = tma_out ? 1 : 0;
+  p.stage_mc = (staged && out.multicast) ? 1 : 0;
   if (p.tma_out)
     for (int d = 0; d < out.n_out; ++d)
       if (!make_out_map(&p.out_maps[d], out.o[d], static_cast<long long>(B) * S, out.H_out * kDim))
@@ -922,9 +969,6 @@ int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
   p.acc = splits > 1 ? static_cast<float*>(workspace) : nullptr;
   p.lsum = splits > 1 ? p.acc + static_cast<size_t>(splits) * rows * kDim : nullptr;
   p.status = status;
-  // The persistent form whenever the CTAs write plain output; the one-item-per-CTA form for the
-  // TMA-staged epilogue, which borrows the Q buffers.
-  const bool persistent = !p.tma_out;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = persistent ? dim3(static_cast<unsigned>(std::min<long long>(items, sms)))
                            : dim3(p.n_pairs, p.BH, splits);
@@ -974,6 +1018,22 @@ int launch_attend_gather(const uint16_t* q, const uint16_t* k, const uint16_t* v
   out.h0 = h0;
   out.n_out = n_out;
   for (int d = 0; d < n_out; ++d) out.o[d] = outs[d];
+  return launch_attend_out(q, k, v, B, H, S, out, splits, workspace, status, stream);
+}
+
+// Merged rows of H_out heads, this call's heads at [h0, h0 + H), stored once through the
+// multicast address `out_mc`, which the NVSwitch replicates into every bound rank's buffer.
+int launch_attend_gather_multicast(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S,
+                                   uint16_t* out_mc, int H_out, int h0, int splits, void* workspace, int* status,
+                                   cudaStream_t stream) {
+  OutLayout out{};
+  out.merged = 1;
+  out.H = H;
+  out.H_out = H_out;
+  out.h0 = h0;
+  out.n_out = 1;
+  out.multicast = 1;
+  out.o[0] = out_mc;
   return launch_attend_out(q, k, v, B, H, S, out, splits, workspace, status, stream);
 }
 

@@ -21,6 +21,9 @@ int launch_attend_layout(const uint16_t* q, const uint16_t* k, const uint16_t* v
 int launch_attend_gather(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S,
                          uint16_t* const* outs, int n_out, int H_out, int h0, int splits, void* workspace,
                          int* status, cudaStream_t stream);
+int launch_attend_gather_multicast(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S,
+                                   uint16_t* out_mc, int H_out, int h0, int splits, void* workspace, int* status,
+                                   cudaStream_t stream);
 int attend_splits(int B, int H, int S, int sms);
 int launch_linear_bf16(const uint16_t* x, const uint16_t* wt, int M, int N, int K, uint16_t* y, int* status, int sms,
                        cudaStream_t stream);
@@ -238,6 +241,31 @@ int flk_attend_gather(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
   }
   return flk::launch_attend_gather(q, k, v, B, H, S, outs, n_outs, H_total, h0, splits, workspace, st->status,
                                    static_cast<cudaStream_t>(stream));
+}
+
+int flk_attend_gather_multicast(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S,
+                                int D, uint16_t* out_mc, int H_total, int h0, void* workspace, size_t ws_bytes,
+                                void* stream) {
+  int err = FLK_OK;
+  if (!attend_shape_ok(B, H, S, D, &err)) return err;
+  if (h0 < 0 || H_total < 1 || static_cast<long long>(h0) + H > H_total) return FLK_ERR_INVALID_ARGUMENT;
+  if (static_cast<long long>(B) * S == 0) return FLK_OK;
+  const void* ptrs[] = {q, k, v, out_mc};
+  for (const void* p : ptrs)
+    if (p == nullptr || !aligned16(p)) return FLK_ERR_INVALID_ARGUMENT;
+  const DeviceState* st = device_state(&err);
+  if (!st) return err;
+  int splits = flk::attend_splits(B, H, S, st->sms);
+  if (splits > 1) {
+    const size_t need = flk::attend_workspace_bytes(B, H, S, splits);
+    if (workspace == nullptr && ws_bytes == 0) {
+      splits = 1;
+    } else if (workspace == nullptr || ws_bytes < need || !aligned16(workspace)) {
+      return FLK_ERR_WORKSPACE;
+    }
+  }
+  return flk::launch_attend_gather_multicast(q, k, v, B, H, S, out_mc, H_total, h0, splits, workspace, st->status,
+                                             static_cast<cudaStream_t>(stream));
 }
 
 int flk_linear(const uint16_t* x, const uint16_t* wt, int M, int N, int K, uint16_t* y, void* stream) {

@@ -10,8 +10,10 @@ the hot path shards without any exchange inside it:
   projection produces), it runs qk_prep + attend locally, and the ranks' heads
   are assembled either by one all-gather (``gather_heads``, then ``merge_heads``)
   or by the attention epilogue itself (``attend_gather_heads``): every rank stores
-  its heads' merged rows straight into every rank's output buffer over NVLink
-  (``PeerOutput``, torch symmetric memory), followed by one barrier.
+  its heads' merged rows into every rank's output buffer over NVLink
+  (``PeerOutput``, torch symmetric memory), followed by one barrier -- once per
+  peer through its pointer, or once through the buffers' NVLink multicast address
+  (multimem stores, replicated by the NVSwitch).
 
 The all-gather runs on whatever process group it is given: NCCL over NVLink on
 the B200 box, gloo in the CPU tests of the layout logic.
@@ -84,13 +86,18 @@ class PeerOutput:
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
-        self.bufs, self.handles, self.ptrs = [], [], []
+        self.bufs, self.handles, self.ptrs, self.mc_ptrs = [], [], [], []
         for _ in range(copies):
             buf = symm_mem.empty(*shape, dtype=torch.bfloat16, device=device)
             handle = symm_mem.rendezvous(buf, group)
             self.bufs.append(buf)
             self.handles.append(handle)
             self.ptrs.append([int(p) for p in handle.buffer_ptrs])
+            self.mc_ptrs.append(int(handle.multicast_ptr))  # 0 where the node has no NVLink multicast
+        # multicast stores need every buffer bound to a multicast object on every rank
+        flag = torch.tensor([1 if all(self.mc_ptrs) else 0], device=device)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+        self.multicast = bool(flag.item())
         self.turn = 0
         self.last = 0  # buffer of the most recent call
 
@@ -101,10 +108,13 @@ class PeerOutput:
 
 
 def attend_gather_heads(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, peer: PeerOutput, h0: int,
-                        num_heads: int, sync: bool = True) -> torch.Tensor:
+                        num_heads: int, sync: bool = True, multicast: bool = False) -> torch.Tensor:
     """Head-sharded attention whose epilogue stores this rank's heads [h0, h0 + H) of the merged
     rows into every rank's buffer; after the barrier, the returned local buffer holds
-    merge_heads(attend(q, k, v)) over all ``num_heads`` heads on every rank. ``sync=False`` leaves
+    merge_heads(attend(q, k, v)) over all ``num_heads`` heads on every rank. The stores go once
+    per rank through the peers' pointers, or, with ``multicast``, once through the buffers'
+    NVLink multicast address (every GPU still receives the whole output either way, so the
+    all-gather stays bound by each GPU's NVLink ingress). ``sync=False`` leaves
     the barrier to the caller (``peer.barrier()``), which must make it before using the buffer
     and before the next call."""
     import ctypes
@@ -118,15 +128,24 @@ def attend_gather_heads(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, peer:
     buf, handle, ptrs = peer.bufs[i], peer.handles[i], peer.ptrs[i]
     if tuple(buf.shape) != (batch, length, num_heads * dim):
         raise ValueError(f"peer buffer {tuple(buf.shape)} is not [B, S, H*D] = {(batch, length, num_heads * dim)}")
-    outs = (ctypes.c_void_p * len(ptrs))(*ptrs)
+    if multicast and not peer.multicast:
+        raise ValueError("these buffers have no NVLink multicast address on every rank")
     lib = _lib.lib()
     with torch.cuda.device(q.device):
         ws_bytes = lib.flk_attend_workspace_size(batch, heads, length, dim)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
-        code = lib.flk_attend_gather(q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, length, dim, outs,
-                                     len(ptrs), num_heads, h0, ws.data_ptr() if ws is not None else None,
-                                     ws_bytes, kernels._stream(q))
-    _lib.check("flk_attend_gather", code)
+        ws_ptr = ws.data_ptr() if ws is not None else None
+        if multicast:
+            name = "flk_attend_gather_multicast"
+            code = lib.flk_attend_gather_multicast(q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, length,
+                                                   dim, peer.mc_ptrs[i], num_heads, h0, ws_ptr, ws_bytes,
+                                                   kernels._stream(q))
+        else:
+            name = "flk_attend_gather"
+            outs = (ctypes.c_void_p * len(ptrs))(*ptrs)
+            code = lib.flk_attend_gather(q.data_ptr(), k.data_ptr(), v.data_ptr(), batch, heads, length, dim, outs,
+                                         len(ptrs), num_heads, h0, ws_ptr, ws_bytes, kernels._stream(q))
+    _lib.check(name, code)
     if sync:
         handle.barrier()
     return buf

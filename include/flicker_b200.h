@@ -103,6 +103,20 @@ int flk_attend_gather(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                       int B, int H, int S, int D, uint16_t* const* outs, int n_outs,
                       int H_total, int h0, void* workspace, size_t ws_bytes, void* stream);
 
+/*
+ * flk_attend_gather with the rows stored once through an NVLink multicast address: out_mc is the
+ * multicast mapping (NVSwitch, e.g. a symmetric-memory buffer's multicast pointer) bound to every
+ * rank's merged output buffer [B, S, H_total * D]; each 16-byte store is a multimem.st, which the
+ * switch writes into all bound buffers, so this rank's heads cross NVLink once instead of once per
+ * peer (the egress of an all-gather drops from (n-1)/n of the output to 1/n of it). Replaces the
+ * same ncclAllGather + merge_heads as flk_attend_gather (src/flicker/modules.py:63-65,157). As
+ * there, the kernel neither waits for nor signals peers: the caller synchronises the ranks after
+ * the call. Same workspace rules as flk_attend, for this call's B, H, S.
+ */
+int flk_attend_gather_multicast(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                int B, int H, int S, int D, uint16_t* out_mc,
+                                int H_total, int h0, void* workspace, size_t ws_bytes, void* stream);
+
 /* Bytes of workspace flk_attend needs for this shape on the current device. */
 size_t flk_attend_workspace_size(int B, int H, int S, int D);
 

@@ -40,17 +40,24 @@ def main() -> int:
         full = fb.attend_merged(*fb.qk_prep(qkv, qs, ks, freqs, H))
         local = sharding.slice_qkv_heads(qkv, H, h0, h1).contiguous()
         q, k, v = fb.qk_prep(local, qs, ks, freqs, h1 - h0)
-        fused = sharding.attend_gather_heads(q, k, v, peer, h0, H).clone()
+        fused = sharding.attend_gather_heads(q, k, v, peer, h0, H, multicast=False).clone()
+        mc = sharding.attend_gather_heads(q, k, v, peer, h0, H, multicast=True).clone() if peer.multicast else None
         o = fb.attend(q, k, v)
         sharding.gather_heads(o, gathered, dist.group.WORLD)
         nccl = sharding.merge_heads(gathered.view(1, H, S, 128))
         torch.cuda.synchronize()
         # the per-rank calls may run split over KV where the all-heads call does not, so they
-        # match it within the attention tolerance; both gathers carry the same per-rank results
+        # match it within the attention tolerance; all gathers carry the same per-rank results
         same = bool(torch.equal(fused, nccl))
         close = (fused.float() - full.float()).abs().max().item() <= 2e-2
         ok &= same and close
         print(f"rank {rank} step {step}: fused == nccl {same}, fused ~ full {close}", flush=True)
+        if mc is not None:
+            mc_same = bool(torch.equal(mc, nccl))
+            ok &= mc_same
+            print(f"rank {rank} step {step}: multicast == nccl {mc_same}", flush=True)
+        else:
+            print(f"rank {rank} step {step}: no NVLink multicast on this node", flush=True)
     status = fb.device_status()
     flag = torch.tensor([1 if (ok and status == 0) else 0], device=dev)
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)

@@ -116,6 +116,16 @@ def test_shape_checks_run_before_any_device_work():
     assert lib.flk_attend_gather(fake, fake, fake, 1, 2, 128, 128, odd_outs, 2, 4, 0, None, 0, None) \
         == _lib.FLK_ERR_INVALID_ARGUMENT
     assert lib.flk_attend_gather(fake, fake, fake, 1, 2, 0, 128, outs, 2, 4, 0, None, 0, None) == 0
+    # gathering attend through a multicast address: one output pointer, heads inside H_total
+    assert lib.flk_attend_gather_multicast(fake, fake, fake, 1, 2, 128, 64, fake, 4, 0, None, 0, None) \
+        == _lib.FLK_ERR_UNSUPPORTED
+    assert lib.flk_attend_gather_multicast(fake, fake, fake, 1, 2, 128, 128, fake, 4, 3, None, 0, None) \
+        == _lib.FLK_ERR_INVALID_ARGUMENT
+    assert lib.flk_attend_gather_multicast(fake, fake, fake, 1, 2, 128, 128, None, 4, 0, None, 0, None) \
+        == _lib.FLK_ERR_INVALID_ARGUMENT
+    assert lib.flk_attend_gather_multicast(fake, fake, fake, 1, 2, 128, 128, odd, 4, 0, None, 0, None) \
+        == _lib.FLK_ERR_INVALID_ARGUMENT
+    assert lib.flk_attend_gather_multicast(fake, fake, fake, 1, 2, 0, 128, fake, 4, 0, None, 0, None) == 0
     # merged-heads attend: the same shape rules as flk_attend
     assert lib.flk_attend_merged(fake, fake, fake, 1, 2, 128, 64, fake, None, 0, None) == _lib.FLK_ERR_UNSUPPORTED
     assert lib.flk_attend_merged(fake, fake, fake, 1, 2, 100, 128, fake, None, 0, None) \
