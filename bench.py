@@ -19,13 +19,14 @@ Multi-GPU (torchrun, one process per GPU, NCCL):
                  batch 8 over 8 GPUs, seed = rank); no data-path collective;
                  weak scaling.
   --shard heads  one batch-1 call split by heads (24/N per rank); strong scaling.
-                 --gather peer (default): the attention epilogue stores each
-                 rank's heads, merged ([1, S, 24*128]), straight into every
-                 rank's output over NVLink (TMA stores into symmetric memory),
-                 then one barrier; --gather multicast: the same rows stored once
-                 through the output buffers' NVLink multicast address (multimem
-                 stores the NVSwitch replicates into every rank's buffer);
-                 --gather nccl: attend, then an NCCL all-gather of
+                 --gather peer: the attention epilogue stores each rank's
+                 heads, merged ([1, S, 24*128]), straight into every rank's
+                 output over NVLink (TMA stores into symmetric memory), then one
+                 barrier; --gather multicast: the same rows stored once through
+                 the output buffers' NVLink multicast address (multimem stores
+                 the NVSwitch replicates into every rank's buffer); --gather
+                 auto (default): multicast from 4 ranks up where available, else
+                 peer; --gather nccl: attend, then an NCCL all-gather of
                  [1, 24/N, S, 128].
   With --shard batch and N > 1 the line also carries `heads_sharded`: the batch-1
   call split by heads, timed the same way in the same run.
@@ -82,9 +83,10 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(GRIDS), default="1024")
     ap.add_argument("--shard", choices=["batch", "heads"], default="batch")
-    ap.add_argument("--gather", choices=["peer", "multicast", "nccl"], default="peer",
+    ap.add_argument("--gather", choices=["auto", "peer", "multicast", "nccl"], default="auto",
                     help="head sharding: epilogue stores into every rank's buffer or through the buffers' "
-                         "multicast address, or an NCCL all-gather")
+                         "multicast address (auto: multicast from 4 ranks up where available), or an NCCL "
+                         "all-gather")
     ap.add_argument("--e2e-steps", type=int, default=None,
                     help=f"steps of the end-to-end leg (default max({E2E_MIN_STEPS}, K/10))")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -755,7 +757,7 @@ def measure_attention(args, torch, dist, fb, sharding, world, rank, dev, group, 
         else:
             gathered = torch.empty((world, 1, heads_local, s, HEAD_DIM), dtype=torch.bfloat16, device=dev)
 
-    use_mc = peer is not None and gather == "multicast"
+    use_mc = peer is not None and (gather == "multicast" or (gather == "auto" and peer.multicast and world >= 4))
 
     def step(i, rec=None):
         qkv, qs, ks, freqs = sets[i % 2]
