@@ -71,6 +71,7 @@ GRIDS = {"512": (32, 32), "1024": (64, 64), "2048": (128, 128)}
 NCU_TRAFFIC_BYTES = {"attend@1024": 89_164_288, "qk_prep@1024": 118_335_744, "w8a8_gemm@config4": 86_272_768}
 NCU_TRAFFIC_NOTE = "ncu dram__bytes_read.sum + dram__bytes_write.sum of one captured launch at this workload"
 E2E_MIN_STEPS = 20  # the end-to-end leg times at least this many steps whatever --steps is
+E2E_REPEATS = 3  # the end-to-end leg reports the median of this many timed runs (all listed)
 CPU_WARMUP, CPU_RUNS = 3, 20  # CPU baseline: median of >= 20 timed runs after 3 warm-ups
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
@@ -873,10 +874,20 @@ def measure_attention(args, torch, dist, fb, sharding, world, rank, dev, group, 
         return o
 
     persistent = peer is not None or gathered is not None
+    barrier = (lambda: dist.barrier()) if world > 1 else None
     pipe.run(2, e2e_compute, persistent_out=persistent)
-    e2e_ms = pipe.run(e2e_steps, e2e_compute, before=(lambda: dist.barrier()) if world > 1 else None,
-                      persistent_out=persistent) * e2e_steps
-    out["e2e_ms"] = max_over_ranks(torch, dist, e2e_ms, dev, world)
+    runs = []
+    for _ in range(E2E_REPEATS):
+        ms = pipe.run(e2e_steps, e2e_compute, before=barrier, persistent_out=persistent) * e2e_steps
+        runs.append(max_over_ranks(torch, dist, ms, dev, world))
+    # The same pipeline with the compute left out: every step's host<->device copies alone, the
+    # floor that the end-to-end time can reach on this box (PCIe and the host's memory, shared
+    # with the other GPUs' jobs, set it).
+    fixed = torch.zeros(out_shape, dtype=torch.bfloat16, device=dev)
+    floor_ms = pipe.run(e2e_steps, lambda d: fixed, before=barrier, persistent_out=persistent) * e2e_steps
+    out["e2e_ms"] = statistics.median(runs)
+    out["e2e_runs_ms"] = runs
+    out["copy_floor_ms"] = max_over_ranks(torch, dist, floor_ms, dev, world)
     out["e2e_steps"] = e2e_steps
     out["h2d"], out["d2h"] = pipe.h2d_bytes, pipe.d2h_bytes
     return out
@@ -971,7 +982,12 @@ def main():
                                  "traffic_source": NCU_TRAFFIC_NOTE, "peak_source": f"{pk_kind} HBM copy"},
             "e2e": {"value": m["total_flops"] * m["e2e_steps"] / (m["e2e_ms"] * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": m["h2d"], "d2h_bytes_per_step": m["d2h"],
-                    "steps": m["e2e_steps"], "ms_per_step": m["e2e_ms"] / m["e2e_steps"]},
+                    "steps": m["e2e_steps"], "ms_per_step": m["e2e_ms"] / m["e2e_steps"],
+                    "runs_ms_per_step": [r / m["e2e_steps"] for r in m["e2e_runs_ms"]],
+                    "copy_floor_ms_per_step": m["copy_floor_ms"] / m["e2e_steps"],
+                    "frac_of_copy_floor": m["copy_floor_ms"] / m["e2e_ms"],
+                    "note": f"median of {E2E_REPEATS} runs of {m['e2e_steps']} steps; the copy floor is the "
+                            "same pipeline with the compute left out"},
             "gpu_launches": (3 if m["split"] else 2) * K,
             "clocks": m["clocks"],
             "device_status": m["status"],
