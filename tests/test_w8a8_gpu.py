@@ -52,9 +52,10 @@ def test_pipeline_bit_exact(m, k, n):
     np.testing.assert_array_equal(to_host(y)[rows].view(np.uint16), yw.view(np.uint16))
 
 
-def test_full_accumulator_tile_columns_and_tail():
-    """Every output element of a multi-tile ragged shape checked (tails in M, N and K)."""
-    m, k, n = 300, 400, 600
+@pytest.mark.parametrize("m,k,n", [(300, 400, 600), (520, 272, 1300), (256, 128, 700)])
+def test_full_accumulator_tile_columns_and_tail(m, k, n):
+    """Every output element of multi-tile ragged shapes checked (tails in M, N and K; several
+    256 x 256 pair tiles per row and column, the last ones mostly past M or N)."""
     rng = np.random.default_rng(1)
     a = rng.integers(-127, 128, (m, k), dtype=np.int8)
     b = rng.integers(-127, 128, (n, k), dtype=np.int8)
