@@ -70,6 +70,13 @@ GRIDS = {"512": (32, 32), "1024": (64, 64), "2048": (128, 128)}
 # kernel's figure can sit below its algorithmic bytes.
 NCU_TRAFFIC_BYTES = {"attend@1024": 89_164_288, "qk_prep@1024": 118_335_744, "w8a8_gemm@config4": 86_272_768}
 NCU_TRAFFIC_NOTE = "ncu dram__bytes_read.sum + dram__bytes_write.sum of one captured launch at this workload"
+# The same counters with the cache left as the bench step leaves it (ncu --cache-control none,
+# application replay; mean of the launches of two timed steps): inside the step a kernel's window
+# also carries the write-back of what the kernel before it left dirty in L2.
+NCU_TRAFFIC_IN_STEP = {"attend@1024": 79_581_824, "qk_prep@1024": 156_495_232,
+                       "w8a8_gemm@config4": 109_930_368, "quantize_act@config4": 47_982_720}
+NCU_TRAFFIC_IN_STEP_NOTE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum inside the bench step "
+                            "(--cache-control none, application replay), mean of two launches")
 E2E_MIN_STEPS = 20  # the end-to-end leg times at least this many steps whatever --steps is
 E2E_REPEATS = 3  # the end-to-end leg reports the median of this many timed runs (all listed)
 CPU_WARMUP, CPU_RUNS = 3, 20  # CPU baseline: median of >= 20 timed runs after 3 warm-ups
@@ -381,11 +388,15 @@ def run_w8a8(args, rank, world):
         "config": {"workload": "W8A8 SmoothQuant linear: per-token quantise + int8 GEMM + dequant", "M": M, "K": K,
                    "N": N, "alpha": 0.5, "outliers": "1% of channels x20",
                    "l2": "2 alternating activation sets; weights (28 MB) L2-resident as in a real layer"},
-        "kernels": {"quantize_act": {"us": q_us, "GB/s": (M * K * 3 + M * 4 + K * 4) / (q_us * 1e-6) / 1e9},
+        "kernels": {"quantize_act": {"us": q_us, "GB/s": (M * K * 3 + M * 4 + K * 4) / (q_us * 1e-6) / 1e9,
+                                     "traffic_in_step": NCU_TRAFFIC_IN_STEP["quantize_act@config4"],
+                                     "traffic_in_step_source": NCU_TRAFFIC_IN_STEP_NOTE},
                     "w8a8_gemm": {"us": g_us, "TOPS": gemm_tops}},
         "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": int8_peak, "unit": "TOPS",
                      "frac": gemm_tops / int8_peak, "traffic": NCU_TRAFFIC_BYTES["w8a8_gemm@config4"],
-                     "traffic_source": NCU_TRAFFIC_NOTE, "kernel": "w8a8_gemm",
+                     "traffic_source": NCU_TRAFFIC_NOTE,
+                     "traffic_in_step": NCU_TRAFFIC_IN_STEP["w8a8_gemm@config4"],
+                     "traffic_in_step_source": NCU_TRAFFIC_IN_STEP_NOTE, "kernel": "w8a8_gemm",
                      "peak_source": "measured here: torch._int_mm (cuBLASLt int8) 8192^3, best of 10, CUDA "
                                     "events; nominal dense int8 4500",
                      "peak_clocks": int8_clocks,
@@ -935,9 +946,9 @@ def main():
     at_tflops = m["flops_local"] / (m["at_ms"] * 1e-3) / 1e12
     qk_gbs = m["bytes_local"] / (m["qk_ms"] * 1e-3) / 1e9
 
-    def traffic(kernel):
+    def traffic(kernel, table=NCU_TRAFFIC_BYTES):
         # captured at the single-GPU 1024^2 call with all 24 heads only
-        return NCU_TRAFFIC_BYTES.get(f"{kernel}@{args.config}") if heads_local == NUM_HEADS else None
+        return table.get(f"{kernel}@{args.config}") if heads_local == NUM_HEADS else None
 
     line = None
     if rank == 0:
@@ -976,10 +987,15 @@ def main():
             "roofline": {"bound": "tensor", "achieved": at_tflops, "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": at_tflops / pk["bf16_tflops"], "traffic": traffic("attend"),
                          "traffic_source": NCU_TRAFFIC_NOTE,
+                         "traffic_in_step": traffic("attend", NCU_TRAFFIC_IN_STEP),
+                         "traffic_in_step_source": NCU_TRAFFIC_IN_STEP_NOTE,
                          "peak_source": f"{pk_kind} bf16 burst (cuBLAS)", "kernel": "attend"},
             "roofline_qk_prep": {"bound": "hbm", "achieved": qk_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s",
                                  "frac": qk_gbs / pk["hbm_gbs"], "traffic": traffic("qk_prep"),
-                                 "traffic_source": NCU_TRAFFIC_NOTE, "peak_source": f"{pk_kind} HBM copy"},
+                                 "traffic_source": NCU_TRAFFIC_NOTE,
+                                 "traffic_in_step": traffic("qk_prep", NCU_TRAFFIC_IN_STEP),
+                                 "traffic_in_step_source": NCU_TRAFFIC_IN_STEP_NOTE,
+                                 "peak_source": f"{pk_kind} HBM copy"},
             "e2e": {"value": m["total_flops"] * m["e2e_steps"] / (m["e2e_ms"] * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": m["h2d"], "d2h_bytes_per_step": m["d2h"],
                     "steps": m["e2e_steps"], "ms_per_step": m["e2e_ms"] / m["e2e_steps"],
