@@ -10,8 +10,9 @@
 // (or one KV split of them). attend_persistent_kernel runs one CTA per SM over many items;
 // attend_kernel runs one item per CTA (kept for the TMA-staged gathering epilogue, which
 // borrows the Q buffers). Warp roles (576 threads, 1 CTA per SM):
-//   warp 0       TMA producer: the item's Q tiles, then K_j, V_j into a 4-slot ring of 32 KB
-//                slots; every fill waits on its buffer's empty barrier (one completion per fill)
+//   warp 0       TMA producer: the item's Q tiles, then K_j, V_j into a ring of four 32 KB
+//                slots (single slots here, slot pairs in the persistent form); every fill waits
+//                on its buffer's empty barrier (one completion per fill)
 //   warp 1       TMEM allocator + UMMA issuer
 //   warps 2-17   softmax: 8 warps per query tile, two per TMEM lane quadrant, each owning 64 of
 //                the 128 columns of its 32 rows: exp + bf16 round, P written back to TMEM in two
@@ -67,7 +68,8 @@ struct alignas(1024) Smem {
   uint64_t kv_full[kSlots];
   // Buffer releases, one arrival (one completion) per fill, so a fill waits for the completion
   // of the fill before it: made by the first softmax warp of the item's last query tile as soon
-  // as it has seen the commit that covers the buffer's last reader (see release_after_s).
+  // as it has seen the commit that covers the buffer's last reader (see release_after_s). The
+  // persistent form uses kv_full/kv_empty[0..1], one per slot pair (a ring stage).
   uint64_t kv_empty[kSlots];
   uint64_t q_empty;  // persistent form: the Q tiles of an item, after its last S
   uint64_t s_full[2];
@@ -181,8 +183,9 @@ __device__ __forceinline__ void row_sum_chunk(const uint32_t (&pk)[16], float2& 
 // columns [64h, 64h+32), i.e. over S columns it has already read.
 __device__ __forceinline__ uint32_t p_col(int kc) { return static_cast<uint32_t>((kc >> 2) * 64 + (kc & 3) * 8); }
 
-// Buffer releases inside an item, made by lane 0 of the first softmax warp of the item's last
-// query tile (nt-1) right after it has seen the commit on s_full[nt-1] that follows S_{nt-1}(j).
+// Buffer releases inside an item of attend_kernel, made by lane 0 of the first softmax warp of the
+// item's last query tile (nt-1) right after it has seen the commit on s_full[nt-1] that follows
+// S_{nt-1}(j).
 // A commit tracks every UMMA issued before it and the issuer runs tile 0's UMMAs of a block
 // before tile 1's, so that commit covers every tile's S(j) -- K_j (ring fill g0 + 2j) is free,
 // and when j is the item's last block, so are the Q tiles -- and every tile's P.V(j-1), issued
@@ -552,7 +555,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 //     i+1 only after they have read O_t of item i (tcgen05.ld + wait), so the issuer's wait for
 //     that P orders the overwrite after the read.
 //   * Q of item i+1 is loaded once S(last) of item i has completed (q_empty, committed right
-//     after that S; no later UMMA of item i reads Q), ring slots as in attend_kernel (kv_empty).
+//     after that S; no later UMMA of item i reads Q).
+// The K/V ring is organised in stages rather than single slots: stage G holds V of the CTA's
+// block G-1 and K of its block G (blocks counted over all of its items), one 64 KB slot pair
+// with one full and one empty barrier. Block j needs exactly V_j and K_{j+1}, i.e. one stage,
+// so the issuer waits once per block instead of twice, and the stage has one release: both its
+// readers (P.V(j-1) and S(j) of every tile) are covered by the commit after S_{nt-1}(j), which
+// the releaser sees -- across an item boundary too, where an item's last V shares its stage with
+// the next item's first K. This measured 2776-2778 cycles per block against 2881-2886 with
+// separate K and V slots (CTA 0, clock64, bench loop), bit-identical output.
 // Used when the CTA itself writes plain (not TMA-staged) output: the TMA-staged epilogue borrows
 // the Q buffers, which this form refills early.
 struct Item {
@@ -616,15 +627,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
     }
-    // Fill f of a buffer (the Q tiles, or a ring slot) waits for completion #(f-1) of its empty
+    // Fill f of a buffer (the Q tiles, or a ring stage) waits for completion #(f-1) of its empty
     // barrier; that barrier cannot complete again before fill f has landed and been read, so the
     // parity wait always refers to its current or its previous phase.
-    uint32_t g = 0, q_fills = 0;  // K/V loads and Q loads issued
+    // Stage G of the ring holds V of the CTA's block G-1 and K of its block G (blocks counted
+    // over all of the CTA's items, so an item's last V shares a stage with the next item's first K);
+    // it fills the slot pair G % 2 (V in slot 2(G % 2), K in slot 2(G % 2) + 1). An item's first
+    // stage goes out before the wait for the Q buffers, so that last V never waits behind Q.
+    uint32_t G = 0, q_fills = 0;  // stages and Q loads issued
     bool ok = true;
+    auto issue_stage = [&](int v_row, int k_row) {
+      const uint32_t sp = G % 2, use = G / 2;
+      if (use > 0 && !mbar_wait_warp(&sm.kv_empty[sp], (use - 1) & 1, abort, p.status)) return false;
+      if (leader) {
+        mbar_arrive_expect_tx(&sm.kv_full[sp], (v_row >= 0 ? kTileBytes : 0) + (k_row >= 0 ? kTileBytes : 0));
+        if (v_row >= 0) {
+          tma_load_2d(sm.kv[2 * sp], &tm_v, 0, v_row, &sm.kv_full[sp]);
+          tma_load_2d(sm.kv[2 * sp] + kHalfBytes, &tm_v, 64, v_row, &sm.kv_full[sp]);
+        }
+        if (k_row >= 0) {
+          tma_load_2d(sm.kv[2 * sp + 1], &tm_k, 0, k_row, &sm.kv_full[sp]);
+          tma_load_2d(sm.kv[2 * sp + 1] + kHalfBytes, &tm_k, 64, k_row, &sm.kv_full[sp]);
+        }
+      }
+      __syncwarp();
+      ++G;
+      return true;
+    };
+    int pending_v = -1;  // row of the previous item's last V, loaded with this item's first K
     for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x) {
       const Item it = decode_item(p, w);
       const int row_base = it.bh * p.S;
-      if (q_fills > 0 && !mbar_wait_warp(&sm.q_empty, (q_fills - 1) & 1, abort, p.status)) break;
+      ok = issue_stage(pending_v, row_base + it.kv0 * kTile);
+      if (!ok) break;
+      if (q_fills > 0 && !mbar_wait_warp(&sm.q_empty, (q_fills - 1) & 1, abort, p.status)) {
+        ok = false;
+        break;
+      }
       if (leader) {
         mbar_arrive_expect_tx(&sm.q_full, it.nt * kTileBytes);
         for (int t = 0; t < it.nt; ++t) {
@@ -635,28 +674,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       ++q_fills;
-      for (int n = 0; n < 2 * it.n_kv; ++n) {
-        const int slot = g % kSlots, fill = g / kSlots;
-        if (fill > 0 && !mbar_wait_warp(&sm.kv_empty[slot], (fill - 1) & 1, abort, p.status)) {
-          ok = false;
-          break;
-        }
-        if (leader) {
-          mbar_arrive_expect_tx(&sm.kv_full[slot], kTileBytes);
-          const void* map = (n & 1) ? static_cast<const void*>(&tm_v) : static_cast<const void*>(&tm_k);
-          const int row = row_base + (it.kv0 + (n >> 1)) * kTile;
-          tma_load_2d(sm.kv[slot], map, 0, row, &sm.kv_full[slot]);
-          tma_load_2d(sm.kv[slot] + kHalfBytes, map, 64, row, &sm.kv_full[slot]);
-        }
-        __syncwarp();
-        ++g;
-      }
+      for (int j = 0; ok && j + 1 < it.n_kv; ++j)
+        ok = issue_stage(row_base + (it.kv0 + j) * kTile, row_base + (it.kv0 + j + 1) * kTile);
+      pending_v = row_base + (it.kv0 + it.n_kv - 1) * kTile;
     }
-    // Never leave with a copy in flight: wait (bounded) for the last fill of Q and of every slot.
+    if (ok && pending_v >= 0) issue_stage(pending_v, -1);  // the last V, alone
+    // Never leave with a copy in flight: wait (bounded) for the last fill of Q and of both stages.
     if (q_fills > 0) mbar_drain(&sm.q_full, (q_fills - 1) & 1, p.status);
-    for (uint32_t s = 0; s < kSlots; ++s) {
-      const uint32_t fills = g > s ? (g - s + kSlots - 1) / kSlots : 0;
-      if (fills > 0) mbar_drain(&sm.kv_full[s], (fills - 1) & 1, p.status);
+    for (uint32_t sp = 0; sp < 2; ++sp) {
+      const uint32_t fills = G > sp ? (G - sp + 1) / 2 : 0;
+      if (fills > 0) mbar_drain(&sm.kv_full[sp], (fills - 1) & 1, p.status);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ UMMA issuer (whole warp, elect.sync issues)
@@ -673,30 +700,31 @@ __global__ void __launch_bounds__(kThreads, 1)
                         kc > 0);
       }
     };
-    uint32_t g0 = 0, items = 0;     // first K/V load of the item, items done
+    uint32_t b0 = 0, items = 0;     // the item's first block (= its first K's stage), items done
     uint32_t blocks[2] = {0, 0};    // KV blocks done per tile: p_part phases consumed
-    auto kv_ready = [&](uint32_t n) { return wait(&sm.kv_full[n % kSlots], (n / kSlots) & 1); };
+    auto stage_ready = [&](uint32_t G) { return wait(&sm.kv_full[G % 2], (G / 2) & 1); };
     bool ok = true;
     for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x) {
       const Item it = decode_item(p, w);
-      ok = wait(&sm.q_full, items & 1) && kv_ready(g0);
+      // stage b0 (this item's first K) was waited for with the previous item's last V
+      ok = wait(&sm.q_full, items & 1) && (b0 > 0 || stage_ready(0));
       if (!ok) break;
       tc_fence_after();
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
         if (t < it.nt) {
-          qk(t, g0 % kSlots);
+          qk(t, 2 * (b0 % 2) + 1);
           tc_commit_warp(&sm.s_full[t]);
         }
       }
-      tc_commit_warp(&sm.kv_empty[g0 % kSlots]);  // K_0 has been read by every tile's S(0)
       for (int j = 0; ok && j < it.n_kv; ++j) {
-        const uint32_t nv = g0 + 2 * j + 1, nk = g0 + 2 * j + 2;
+        const uint32_t st = b0 + j + 1;  // V_j and K_{j+1} (or the next item's first K)
         const bool last = (j == it.n_kv - 1);
-        ok = kv_ready(nv) && (last || kv_ready(nk));
+        ok = stage_ready(st);
         if (!ok) break;
-        const uint32_t vslot = v_lo + (nv % kSlots) * kTile16;
-        const int kslot = nk % kSlots;
+        tc_fence_after();
+        const uint32_t vslot = v_lo + (2 * (st % 2)) * kTile16;
+        const int kslot = 2 * (st % 2) + 1;
 #pragma unroll
         for (int t = 0; t < 2; ++t) {
           if (t >= it.nt) break;
@@ -714,7 +742,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (!ok) break;
           if (last) {
-            if (t == it.nt - 1) tc_commit_warp(&sm.kv_empty[nv % kSlots]);  // the last V, read by every tile
             tc_commit_warp(&sm.o_full[t]);
             continue;
           }
@@ -723,7 +750,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       for (int t = 0; t < it.nt; ++t) blocks[t] += it.n_kv;
-      g0 += 2 * it.n_kv;
+      b0 += it.n_kv;
       ++items;
     }
     tc_commit_warp(&sm.drain);
@@ -739,21 +766,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t s_addr = tmem + lane_off + t * 128 + half * 64;
     const uint32_t o_addr = tmem + lane_off + 256 + t * 128 + half * 64;
     uint32_t s_seen = 0, o_seen = 0, items = 0;  // s_full[t] / o_full[t] completions consumed, items of tile t
-    uint32_t g0 = 0;                             // ring index of the item's first K/V load
+    uint32_t g0 = 0;                             // the item's first block (its first K's stage)
     // Once a wait has failed the warp does no more work, but it still meets its tile's named
     // barrier once per item, as its partner warps (which may not have seen the failure yet) do.
     bool ok = true;
     for (int w = blockIdx.x; w < p.n_items; w += gridDim.x) {
       const Item it = decode_item(p, w);
       const uint32_t item_g0 = g0;
-      g0 += 2 * it.n_kv;
+      g0 += it.n_kv;
       if (t >= it.nt) continue;
       const bool releaser = t == it.nt - 1 && sw % kSoftmaxWarps == 0 && lane == 0;
       float2 l0 = make_float2(0.f, 0.f), l1 = make_float2(0.f, 0.f);
       for (int j = 0; ok && j < it.n_kv; ++j, ++s_seen) {
         ok = mbar_wait_warp(&sm.s_full[t], s_seen & 1, abort, p.status);
         if (!ok) break;
-        if (releaser) release_after_s(sm, item_g0, j, it.n_kv);
+        if (releaser) {
+          // S(j) of every tile is done, and so is every P.V issued before it: stage b0 + j
+          // (V of the block before, K_j) is free
+          mbar_arrive(&sm.kv_empty[(item_g0 + j) % 2]);
+          if (j == it.n_kv - 1) mbar_arrive(&sm.q_empty);
+        }
         tc_fence_after();
         uint32_t ra[32], rb[32], pk0[16], pk1[16];
         tmem_ld_32x32b_x32(s_addr, ra);

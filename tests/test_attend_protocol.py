@@ -3,14 +3,16 @@
 The kernel's three roles are restated as Python generators that yield their waits, in the same
 order and with the same completion indices as the CUDA code:
 
-* the producer (TMA warp): per item the Q tiles, then K_0, V_0, K_1, ... into a 4-slot ring;
-  fill f of a buffer waits for completion #(f-1) of its empty barrier (q_empty, kv_empty[slot]);
-* the issuer (UMMA warp): S_t(0), then per KV block P.V_t(j) in two chunks and S_t(j+1), with
-  commits on s_full[t] and, after an item's last block, on o_full[t];
+* the producer (TMA warp): a ring of two stages (slot pairs); stage G holds V of the CTA's block
+  G-1 and K of its block G, blocks counted over all of its items, so an item's first stage (its
+  K_0 with the previous item's last V) goes out before the wait for the Q buffers; fill f of a
+  buffer waits for completion #(f-1) of its empty barrier (q_empty, kv_empty[stage]);
+* the issuer (UMMA warp): S_t(0), then per KV block one wait for stage b0 + j + 1 (V_j, K_{j+1}),
+  P.V_t(j) in two chunks and S_t(j+1), with commits on s_full[t] and, after an item's last
+  block, on o_full[t];
 * 16 softmax warps: exp of S into P (two hand-over chunks), the row-sum exchange over a named
   barrier (double-buffered by item parity) and the epilogue read of O; one warp of the item's
-  last query tile releases the buffers inside an item (release_after_s) as it sees commits, the
-  issuer commits the releases of an item's first K and last V itself.
+  last query tile releases stage b0 + j (and, at the last block, Q) as it sees S(j) complete.
 
 The 'hardware' runs at random times: TMA copies land, UMMAs execute in issue order, commits
 arrive. mbarrier waits use the hardware's parity semantics (a wait for parity p returns once the
@@ -56,11 +58,11 @@ def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, release_from_tile0
     n_items = bh * ((n_tiles + 1) // 2) * n_splits
     items = [decode(w, n_tiles, n_splits) for w in range(cta, n_items, grid)]
     q_full = Bar("q_full")
-    kv_full = [Bar(f"kv_full{s}") for s in range(4)]
+    kv_full = [Bar(f"kv_full{s}") for s in range(2)]
     s_full = [Bar(f"s_full{t}") for t in range(2)]
     p_part = [[Bar(f"p_part{t}{c}", 8) for c in range(2)] for t in range(2)]
     o_full = [Bar(f"o_full{t}") for t in range(2)]
-    kv_empty = [Bar(f"kv_empty{s}") for s in range(4)]
+    kv_empty = [Bar(f"kv_empty{s}") for s in range(2)]
     q_empty = Bar("q_empty")
     qbuf, q_inflight = [None, None], [False, False]
     kv, kv_inflight = [None] * 4, [False] * 4
@@ -80,8 +82,24 @@ def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, release_from_tile0
         return done
 
     def producer():
-        g = q_fills = 0
+        stage = [0]
+        q_fills = 0
+
+        def issue(v, k):  # stage G: v into slot 2 (G % 2), k into slot 2 (G % 2) + 1
+            sp, use = stage[0] % 2, stage[0] // 2
+            if use > 0:
+                yield ("wait", kv_empty[sp], use - 1)
+            for slot, tile in ((2 * sp, v), (2 * sp + 1, k)):
+                if tile is not None:
+                    if kv_inflight[slot]:
+                        raise ProtocolError("slot refilled while a copy into it is in flight")
+                    kv_inflight[slot] = True
+            tma.append(("kv", sp, v, k))
+            stage[0] += 1
+
+        pending_v = None  # the previous item's last V, loaded with this item's first K
         for it in items:
+            yield from issue(pending_v, ("K", it["w"], 0))
             if q_fills > 0:
                 yield ("wait", q_empty, q_fills - 1)
             if any(q_inflight):
@@ -90,53 +108,45 @@ def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, release_from_tile0
                 q_inflight[t] = True
             tma.append(("q", it["w"], it["nt"]))
             q_fills += 1
-            for n in range(2 * it["n_kv"]):
-                slot, fill = g % 4, g // 4
-                if fill > 0:
-                    yield ("wait", kv_empty[slot], fill - 1)
-                if kv_inflight[slot]:
-                    raise ProtocolError("slot refilled while a copy into it is in flight")
-                kv_inflight[slot] = True
-                tma.append(("kv", slot, ("V" if n & 1 else "K", it["w"], n >> 1)))
-                g += 1
+            for j in range(it["n_kv"] - 1):
+                yield from issue(("V", it["w"], j), ("K", it["w"], j + 1))
+            pending_v = ("V", it["w"], it["n_kv"] - 1)
+        if pending_v is not None:
+            yield from issue(pending_v, None)
 
     def issuer():
-        g0, done, blocks = 0, 0, [0, 0]
+        b0, done, blocks = 0, 0, [0, 0]
         for it in items:
             yield ("wait", q_full, done)
-            yield ("wait", kv_full[g0 % 4], g0 // 4)
+            if b0 == 0:  # later items' first stage was waited for with the previous item's last V
+                yield ("wait", kv_full[0], 0)
             for t in range(it["nt"]):
-                mma.append(("S", it["w"], t, 0, g0 % 4))
+                mma.append(("S", it["w"], t, 0, 2 * (b0 % 2) + 1))
                 mma.append(("commit", s_full[t]))
-            mma.append(("commit", kv_empty[g0 % 4]))
             n_kv = it["n_kv"]
             for j in range(n_kv):
-                nv, nk = g0 + 2 * j + 1, g0 + 2 * j + 2
+                st = b0 + j + 1
                 last = j == n_kv - 1
-                yield ("wait", kv_full[nv % 4], nv // 4)
-                if not last:
-                    yield ("wait", kv_full[nk % 4], nk // 4)
+                yield ("wait", kv_full[st % 2], st // 2)
                 for t in range(it["nt"]):
                     for c in range(2):
                         yield ("wait", p_part[t][c], blocks[t] + j)
-                        mma.append(("PV", it["w"], t, j, c, nv % 4))
+                        mma.append(("PV", it["w"], t, j, c, 2 * (st % 2)))
                     if last:
-                        if t == it["nt"] - 1:
-                            mma.append(("commit", kv_empty[nv % 4]))
                         mma.append(("commit", o_full[t]))
                     else:
-                        mma.append(("S", it["w"], t, j + 1, nk % 4))
+                        mma.append(("S", it["w"], t, j + 1, 2 * (st % 2) + 1))
                         mma.append(("commit", s_full[t]))
             for t in range(it["nt"]):
                 blocks[t] += n_kv
-            g0 += 2 * n_kv
+            b0 += n_kv
             done += 1
 
     def softmax(t, quad, half):
-        s_seen = o_seen = n_done = g0 = 0
+        s_seen = o_seen = n_done = b0 = 0
         for it in items:
-            item_g0 = g0
-            g0 += 2 * it["n_kv"]
+            item_b0 = b0
+            b0 += it["n_kv"]
             if t >= it["nt"]:
                 continue
             n_kv = it["n_kv"]
@@ -146,9 +156,7 @@ def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, release_from_tile0
                 yield ("wait", s_full[t], s_seen)
                 s_seen += 1
                 if releaser:
-                    if j > 0:
-                        kv_empty[(item_g0 + 2 * j) % 4].arrive()
-                        kv_empty[(item_g0 + 2 * j - 1) % 4].arrive()
+                    kv_empty[(item_b0 + j) % 2].arrive()  # stage b0 + j: V_{j-1} (or the last V before) and K_j
                     if j == n_kv - 1:
                         q_empty.arrive()
                 if s_reg[t][quad][half] != ("S", it["w"], t, j):
@@ -207,8 +215,11 @@ def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, release_from_tile0
                 qbuf[t], q_inflight[t] = e[1], False
             q_full.arrive()
         else:
-            kv[e[1]], kv_inflight[e[1]] = e[2], False
-            kv_full[e[1]].arrive()
+            _, sp, v, k = e
+            for slot, tile in ((2 * sp, v), (2 * sp + 1, k)):
+                if tile is not None:
+                    kv[slot], kv_inflight[slot] = tile, False
+            kv_full[sp].arrive()
 
     agents = [producer(), issuer()] + [softmax(t, q, h) for t in range(2) for q in range(4) for h in range(2)]
     req = [None] * len(agents)
