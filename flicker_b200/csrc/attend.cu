@@ -10,15 +10,16 @@
 // (or one KV split of them). attend_persistent_kernel runs one CTA per SM over many items;
 // attend_kernel runs one item per CTA (kept for the TMA-staged gathering epilogue, which
 // borrows the Q buffers). Warp roles (576 threads, 1 CTA per SM):
-//   warp 0       TMA producer: the item's Q tiles, then K_j, V_j into a ring of four 32 KB
-//                slots (single slots here, slot pairs in the persistent form); every fill waits
-//                on its buffer's empty barrier (one completion per fill)
+//   warp 0       TMA producer: the item's Q tiles, then the K/V ring in stages -- stage j holds
+//                V_{j-1} and K_j in a pair of 32 KB slots, two pairs -- so that the issuer waits
+//                once per KV block; every fill waits on its buffer's empty barrier (one
+//                completion per fill)
 //   warp 1       TMEM allocator + UMMA issuer
 //   warps 2-17   softmax: 8 warps per query tile, two per TMEM lane quadrant, each owning 64 of
 //                the 128 columns of its 32 rows: exp + bf16 round, P written back to TMEM in two
 //                32-column chunks (each handed to the issuer with one arrival per warp), row
 //                sums; then the epilogue O / l -> bf16 -> global (or fp32 partials for a split).
-//                One of them also releases ring slots and Q as it sees the commits (see
+//                One of them also releases ring stages and Q as it sees the commits (see
 //                release_after_s).
 // The producer and issuer warps run converged: all 32 lanes walk the loop and wait on the
 // barriers with one warp-wide vote per wait; lane 0 issues the TMA loads and elect.sync picks
@@ -50,7 +51,8 @@ namespace {
 
 constexpr int kTile = 128;                 // query rows per tile, KV rows per block
 constexpr int kDim = 128;                  // head dim
-constexpr int kSlots = 4;                  // K/V ring slots (K_j, V_j alternate; 2 blocks of lookahead)
+constexpr int kSlots = 4;                  // K/V ring slots of 32 KB, in kStages pairs
+constexpr int kStages = 2;                 // ring stages: V_{j-1} + K_j each; 2 blocks of lookahead
 constexpr int kTileBytes = kTile * kDim * 2;  // 32 KB: one bf16 128 x 128 tile
 constexpr int kHalfBytes = kTileBytes / 2;    // one 64-column TMA box (128 B rows)
 constexpr int kSoftmaxWarps = 8;           // per query tile: 2 per TMEM lane quadrant
@@ -65,12 +67,11 @@ struct alignas(1024) Smem {
   uint8_t q[2][kTileBytes];
   uint8_t kv[kSlots][kTileBytes];
   uint64_t q_full;
-  uint64_t kv_full[kSlots];
+  uint64_t kv_full[kStages];
   // Buffer releases, one arrival (one completion) per fill, so a fill waits for the completion
   // of the fill before it: made by the first softmax warp of the item's last query tile as soon
-  // as it has seen the commit that covers the buffer's last reader (see release_after_s). The
-  // persistent form uses kv_full/kv_empty[0..1], one per slot pair (a ring stage).
-  uint64_t kv_empty[kSlots];
+  // as it has seen the commit that covers the buffer's last readers (see release_after_s).
+  uint64_t kv_empty[kStages];
   uint64_t q_empty;  // persistent form: the Q tiles of an item, after its last S
   uint64_t s_full[2];
   uint64_t p_part[2][2];  // [tile][column chunk]: P chunk c of every softmax warp of the tile is in TMEM
@@ -183,22 +184,15 @@ __device__ __forceinline__ void row_sum_chunk(const uint32_t (&pk)[16], float2& 
 // columns [64h, 64h+32), i.e. over S columns it has already read.
 __device__ __forceinline__ uint32_t p_col(int kc) { return static_cast<uint32_t>((kc >> 2) * 64 + (kc & 3) * 8); }
 
-// Buffer releases inside an item of attend_kernel, made by lane 0 of the first softmax warp of the
-// item's last query tile (nt-1) right after it has seen the commit on s_full[nt-1] that follows
-// S_{nt-1}(j).
-// A commit tracks every UMMA issued before it and the issuer runs tile 0's UMMAs of a block
-// before tile 1's, so that commit covers every tile's S(j) -- K_j (ring fill g0 + 2j) is free,
-// and when j is the item's last block, so are the Q tiles -- and every tile's P.V(j-1), issued
-// before S(j): V_{j-1} (fill g0 + 2j - 1). g0 is the ring index of the item's first K/V load.
-// The item's first K and last V are released by the issuer's own commits (kv_empty right after
-// S_{nt-1}(0) and after P.V_{nt-1}(last)): at those two points the softmax warps are busy with
-// the previous item's epilogue or their row sums, and a late release would hold up the refills.
-__device__ __forceinline__ void release_after_s(Smem& sm, uint32_t g0, int j, int n_kv) {
-  if (j > 0) {
-    mbar_arrive(&sm.kv_empty[(g0 + 2 * j) % kSlots]);
-    mbar_arrive(&sm.kv_empty[(g0 + 2 * j - 1) % kSlots]);
-  }
-  if (j == n_kv - 1) mbar_arrive(&sm.q_empty);
+// Buffer releases, made by lane 0 of the first softmax warp of the item's last query tile (nt-1)
+// right after it has seen the commit on s_full[nt-1] that follows S_{nt-1}(j). A commit tracks
+// every UMMA issued before it and the issuer runs tile 0's UMMAs of a block before tile 1's, so
+// that commit covers every tile's S(j) and every tile's P.V(j-1), issued before S(j). Those are
+// the two readers of ring stage `stage` (V of the block before and K_j), which is therefore
+// free; when j is the item's last block, so are the Q tiles.
+__device__ __forceinline__ void release_after_s(Smem& sm, uint32_t stage, bool last_block) {
+  mbar_arrive(&sm.kv_empty[stage % 2]);
+  if (last_block) mbar_arrive(&sm.q_empty);
 }
 
 // 128-column output row that holds query row `grow` (= (b * H + h) * S + s): itself in the
@@ -348,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
-    for (int s = 0; s < kSlots; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.kv_full[s], 1);
       mbar_init(&sm.kv_empty[s], 1);
     }
@@ -390,31 +384,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(sm.q[t] + kHalfBytes, &tm_q, 64, row, &sm.q_full);
       }
     }
-    // Fill f of a ring slot waits for completion #(f-1) of the slot's kv_empty. That barrier
+    // The K/V ring runs in stages: stage j holds V_{j-1} and K_j (stage 0 only K_0, stage n_kv only
+    // the last V) in slot pair j % 2 (V in slot 2(j % 2), K in slot 2(j % 2) + 1), one full and one
+    // empty barrier per pair. Fill f of a pair waits for completion #(f-1) of its kv_empty, which
     // cannot complete again before this fill has landed and been read, so the parity wait always
     // refers to its current or its previous phase, however late this warp runs.
-    int issued[kSlots] = {};
-    for (int n = 0; n < 2 * n_kv; ++n) {
-      const int slot = n % kSlots, fill = n / kSlots;
-      if (fill > 0 && !mbar_wait_warp(&sm.kv_empty[slot], (fill - 1) & 1, abort, p.status)) break;
+    uint32_t G = 0;
+    bool ok = true;
+    auto issue_stage = [&](int v_row, int k_row) {
+      const uint32_t sp = G % 2, use = G / 2;
+      if (use > 0 && !mbar_wait_warp(&sm.kv_empty[sp], (use - 1) & 1, abort, p.status)) return false;
       if (leader) {
-        mbar_arrive_expect_tx(&sm.kv_full[slot], kTileBytes);
-        const void* map = (n & 1) ? static_cast<const void*>(&tm_v) : static_cast<const void*>(&tm_k);
-        const int row = row_base + (kv0 + (n >> 1)) * kTile;
-        tma_load_2d(sm.kv[slot], map, 0, row, &sm.kv_full[slot]);
-        tma_load_2d(sm.kv[slot] + kHalfBytes, map, 64, row, &sm.kv_full[slot]);
+        mbar_arrive_expect_tx(&sm.kv_full[sp], (v_row >= 0 ? kTileBytes : 0) + (k_row >= 0 ? kTileBytes : 0));
+        if (v_row >= 0) {
+          tma_load_2d(sm.kv[2 * sp], &tm_v, 0, v_row, &sm.kv_full[sp]);
+          tma_load_2d(sm.kv[2 * sp] + kHalfBytes, &tm_v, 64, v_row, &sm.kv_full[sp]);
+        }
+        if (k_row >= 0) {
+          tma_load_2d(sm.kv[2 * sp + 1], &tm_k, 0, k_row, &sm.kv_full[sp]);
+          tma_load_2d(sm.kv[2 * sp + 1] + kHalfBytes, &tm_k, 64, k_row, &sm.kv_full[sp]);
+        }
       }
-      issued[slot] = n / kSlots + 1;
       __syncwarp();
-    }
-    // Never leave with a copy in flight: wait (bounded) for the last fill of every slot.
+      ++G;
+      return true;
+    };
+    for (int j = 0; ok && j <= n_kv; ++j)
+      ok = issue_stage(j > 0 ? row_base + (kv0 + j - 1) * kTile : -1, j < n_kv ? row_base + (kv0 + j) * kTile : -1);
+    // Never leave with a copy in flight: wait (bounded) for the last fill of Q and of both pairs.
     mbar_drain(&sm.q_full, 0, p.status);
-    for (int s = 0; s < kSlots; ++s)
-      if (issued[s] > 0) mbar_drain(&sm.kv_full[s], (issued[s] - 1) & 1, p.status);
+    for (uint32_t sp = 0; sp < 2; ++sp) {
+      const uint32_t fills = G > sp ? (G - sp + 1) / 2 : 0;
+      if (fills > 0) mbar_drain(&sm.kv_full[sp], (fills - 1) & 1, p.status);
+    }
   } else if (warp == 1) {
     // ------------------------------------------------------------ UMMA issuer (whole warp, elect.sync issues)
     auto wait = [&](uint64_t* bar, uint32_t parity) { return mbar_wait_warp(bar, parity, abort, p.status); };
-    auto kv_ready = [&](int n) { return wait(&sm.kv_full[n % kSlots], (n / kSlots) & 1); };
+    auto stage_ready = [&](int st) { return wait(&sm.kv_full[st % 2], (st / 2) & 1); };
     // Descriptor low words: Q tile t, K-major ring slot, MN-major (V) ring slot; chunk kc, slot and
     // tile offsets are added to the start field (units of 16 bytes).
     const uint32_t q_lo = umma_desc_lo(smem_u32(sm.q[0]), 16);
@@ -429,25 +435,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                         kc > 0);
       }
     };
-    bool ok = wait(&sm.q_full, 0) && kv_ready(0);
+    bool ok = wait(&sm.q_full, 0) && stage_ready(0);
     if (ok) {
       tc_fence_after();
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
         if (t < nt) {
-          qk(t, 0);  // S_t(0) = Q_t K_0^T
+          qk(t, 1);  // S_t(0) = Q_t K_0^T (stage 0, K slot of pair 0)
           tc_commit_warp(&sm.s_full[t]);
         }
       }
-      tc_commit_warp(&sm.kv_empty[0]);  // K_0 has been read by every tile's S(0)
     }
     for (int j = 0; ok && j < n_kv; ++j) {
-      const int nv = 2 * j + 1, nk = 2 * j + 2;
+      const int st = j + 1;  // V_j and K_{j+1}
       const bool last = (j == n_kv - 1);
-      ok = kv_ready(nv) && (last || kv_ready(nk));
+      ok = stage_ready(st);
       if (!ok) break;
-      const uint32_t vslot = v_lo + (nv % kSlots) * kTile16;
-      const int kslot = nk % kSlots;
+      const uint32_t vslot = v_lo + (2 * (st % 2)) * kTile16;
+      const int kslot = 2 * (st % 2) + 1;
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
         if (t >= nt) break;
@@ -467,7 +472,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         if (last) {
-          if (t == nt - 1) tc_commit_warp(&sm.kv_empty[nv % kSlots]);  // the last V, read by every tile
           tc_commit_warp(&sm.o_full[t]);
           continue;
         }
@@ -496,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Warp-uniform outcome: the tcgen05.ld/st below are .sync.aligned.
         ok = mbar_wait_warp(&sm.s_full[t], j & 1, abort, p.status);
         if (!ok) break;
-        if (releaser) release_after_s(sm, 0, j, n_kv);
+        if (releaser) release_after_s(sm, j, j == n_kv - 1);
         tc_fence_after();
         // Two 32-column chunks of this row's half of S; chunk 1 is loading while chunk 0 is
         // exponentiated, and each chunk's P is handed to the issuer as soon as it is in TMEM.
@@ -556,14 +560,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 //     that P orders the overwrite after the read.
 //   * Q of item i+1 is loaded once S(last) of item i has completed (q_empty, committed right
 //     after that S; no later UMMA of item i reads Q).
-// The K/V ring is organised in stages rather than single slots: stage G holds V of the CTA's
-// block G-1 and K of its block G (blocks counted over all of its items), one 64 KB slot pair
-// with one full and one empty barrier. Block j needs exactly V_j and K_{j+1}, i.e. one stage,
-// so the issuer waits once per block instead of twice, and the stage has one release: both its
-// readers (P.V(j-1) and S(j) of every tile) are covered by the commit after S_{nt-1}(j), which
-// the releaser sees -- across an item boundary too, where an item's last V shares its stage with
-// the next item's first K. This measured 2776-2778 cycles per block against 2881-2886 with
-// separate K and V slots (CTA 0, clock64, bench loop), bit-identical output.
+// The K/V ring stages count blocks over all of the CTA's items: stage G holds V of its block G-1
+// and K of its block G, so an item's last V shares a stage with the next item's first K, and the
+// release after S(0) of the next item covers both (the last P.V of an item is issued before the
+// next item's S(0)). Block j needs exactly V_j and K_{j+1}, one stage, so the issuer waits once
+// per block instead of twice (separate K and V slots): 2776-2778 cycles per block against
+// 2881-2886 (CTA 0, clock64, bench loop), bit-identical output.
 // Used when the CTA itself writes plain (not TMA-staged) output: the TMA-staged epilogue borrows
 // the Q buffers, which this form refills early.
 struct Item {
@@ -594,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 1);
-    for (int s = 0; s < kSlots; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&sm.kv_full[s], 1);
       mbar_init(&sm.kv_empty[s], 1);
     }
@@ -780,12 +782,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; ok && j < it.n_kv; ++j, ++s_seen) {
         ok = mbar_wait_warp(&sm.s_full[t], s_seen & 1, abort, p.status);
         if (!ok) break;
-        if (releaser) {
-          // S(j) of every tile is done, and so is every P.V issued before it: stage b0 + j
-          // (V of the block before, K_j) is free
-          mbar_arrive(&sm.kv_empty[(item_g0 + j) % 2]);
-          if (j == it.n_kv - 1) mbar_arrive(&sm.q_empty);
-        }
+        if (releaser) release_after_s(sm, item_g0 + j, j == it.n_kv - 1);
         tc_fence_after();
         uint32_t ra[32], rb[32], pk0[16], pk1[16];
         tmem_ld_32x32b_x32(s_addr, ra);
