@@ -195,6 +195,37 @@ __device__ __forceinline__ void release_after_s(Smem& sm, uint32_t stage, bool l
   if (last_block) mbar_arrive(&sm.q_empty);
 }
 
+// Issues ring stage G (and advances G): V rows `v_row` into the pair's V slot and K rows `k_row`
+// into its K slot (a negative row leaves that half out), once the stage's previous fill has been
+// released. The whole producer warp calls it; lane 0 (`leader`) issues the copies.
+__device__ __forceinline__ bool issue_kv_stage(Smem& sm, const CUtensorMap* tm_k, const CUtensorMap* tm_v, uint32_t& G,
+                                               int v_row, int k_row, bool leader, volatile int* abort, int* status) {
+  const uint32_t sp = G % kStages, use = G / kStages;
+  if (use > 0 && !mbar_wait_warp(&sm.kv_empty[sp], (use - 1) & 1, abort, status)) return false;
+  if (leader) {
+    mbar_arrive_expect_tx(&sm.kv_full[sp], (v_row >= 0 ? kTileBytes : 0) + (k_row >= 0 ? kTileBytes : 0));
+    if (v_row >= 0) {
+      tma_load_2d(sm.kv[2 * sp], tm_v, 0, v_row, &sm.kv_full[sp]);
+      tma_load_2d(sm.kv[2 * sp] + kHalfBytes, tm_v, 64, v_row, &sm.kv_full[sp]);
+    }
+    if (k_row >= 0) {
+      tma_load_2d(sm.kv[2 * sp + 1], tm_k, 0, k_row, &sm.kv_full[sp]);
+      tma_load_2d(sm.kv[2 * sp + 1] + kHalfBytes, tm_k, 64, k_row, &sm.kv_full[sp]);
+    }
+  }
+  __syncwarp();
+  ++G;
+  return true;
+}
+
+// Never leave with a copy in flight: wait (bounded) for the last of the G stage fills on each pair.
+__device__ __forceinline__ void drain_kv_stages(Smem& sm, uint32_t G, int* status) {
+  for (uint32_t sp = 0; sp < kStages; ++sp) {
+    const uint32_t fills = G > sp ? (G - sp + kStages - 1) / kStages : 0;
+    if (fills > 0) mbar_drain(&sm.kv_full[sp], (fills - 1) & 1, status);
+  }
+}
+
 // 128-column output row that holds query row `grow` (= (b * H + h) * S + s): itself in the
 // head-major layout; (b * S + s) * H_out + h0 + h when heads are merged (modules.merge_heads,
 // src/flicker/modules.py:63-65).
@@ -392,31 +423,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t G = 0;
     bool ok = true;
     auto issue_stage = [&](int v_row, int k_row) {
-      const uint32_t sp = G % 2, use = G / 2;
-      if (use > 0 && !mbar_wait_warp(&sm.kv_empty[sp], (use - 1) & 1, abort, p.status)) return false;
-      if (leader) {
-        mbar_arrive_expect_tx(&sm.kv_full[sp], (v_row >= 0 ? kTileBytes : 0) + (k_row >= 0 ? kTileBytes : 0));
-        if (v_row >= 0) {
-          tma_load_2d(sm.kv[2 * sp], &tm_v, 0, v_row, &sm.kv_full[sp]);
-          tma_load_2d(sm.kv[2 * sp] + kHalfBytes, &tm_v, 64, v_row, &sm.kv_full[sp]);
-        }
-        if (k_row >= 0) {
-          tma_load_2d(sm.kv[2 * sp + 1], &tm_k, 0, k_row, &sm.kv_full[sp]);
-          tma_load_2d(sm.kv[2 * sp + 1] + kHalfBytes, &tm_k, 64, k_row, &sm.kv_full[sp]);
-        }
-      }
-      __syncwarp();
-      ++G;
-      return true;
+      return issue_kv_stage(sm, &tm_k, &tm_v, G, v_row, k_row, leader, abort, p.status);
     };
     for (int j = 0; ok && j <= n_kv; ++j)
       ok = issue_stage(j > 0 ? row_base + (kv0 + j - 1) * kTile : -1, j < n_kv ? row_base + (kv0 + j) * kTile : -1);
     // Never leave with a copy in flight: wait (bounded) for the last fill of Q and of both pairs.
     mbar_drain(&sm.q_full, 0, p.status);
-    for (uint32_t sp = 0; sp < 2; ++sp) {
-      const uint32_t fills = G > sp ? (G - sp + 1) / 2 : 0;
-      if (fills > 0) mbar_drain(&sm.kv_full[sp], (fills - 1) & 1, p.status);
-    }
+    drain_kv_stages(sm, G, p.status);
   } else if (warp == 1) {
     // ------------------------------------------------------------ UMMA issuer (whole warp, elect.sync issues)
     auto wait = [&](uint64_t* bar, uint32_t parity) { return mbar_wait_warp(bar, parity, abort, p.status); };
@@ -639,22 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t G = 0, q_fills = 0;  // stages and Q loads issued
     bool ok = true;
     auto issue_stage = [&](int v_row, int k_row) {
-      const uint32_t sp = G % 2, use = G / 2;
-      if (use > 0 && !mbar_wait_warp(&sm.kv_empty[sp], (use - 1) & 1, abort, p.status)) return false;
-      if (leader) {
-        mbar_arrive_expect_tx(&sm.kv_full[sp], (v_row >= 0 ? kTileBytes : 0) + (k_row >= 0 ? kTileBytes : 0));
-        if (v_row >= 0) {
-          tma_load_2d(sm.kv[2 * sp], &tm_v, 0, v_row, &sm.kv_full[sp]);
-          tma_load_2d(sm.kv[2 * sp] + kHalfBytes, &tm_v, 64, v_row, &sm.kv_full[sp]);
-        }
-        if (k_row >= 0) {
-          tma_load_2d(sm.kv[2 * sp + 1], &tm_k, 0, k_row, &sm.kv_full[sp]);
-          tma_load_2d(sm.kv[2 * sp + 1] + kHalfBytes, &tm_k, 64, k_row, &sm.kv_full[sp]);
-        }
-      }
-      __syncwarp();
-      ++G;
-      return true;
+      return issue_kv_stage(sm, &tm_k, &tm_v, G, v_row, k_row, leader, abort, p.status);
     };
     int pending_v = -1;  // row of the previous item's last V, loaded with this item's first K
     for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x) {
@@ -683,10 +681,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && pending_v >= 0) issue_stage(pending_v, -1);  // the last V, alone
     // Never leave with a copy in flight: wait (bounded) for the last fill of Q and of both stages.
     if (q_fills > 0) mbar_drain(&sm.q_full, (q_fills - 1) & 1, p.status);
-    for (uint32_t sp = 0; sp < 2; ++sp) {
-      const uint32_t fills = G > sp ? (G - sp + 1) / 2 : 0;
-      if (fills > 0) mbar_drain(&sm.kv_full[sp], (fills - 1) & 1, p.status);
-    }
+    drain_kv_stages(sm, G, p.status);
   } else if (warp == 1) {
     // ------------------------------------------------------------ UMMA issuer (whole warp, elect.sync issues)
     auto wait = [&](uint64_t* bar, uint32_t parity) { return mbar_wait_warp(bar, parity, abort, p.status); };
