@@ -185,7 +185,8 @@ __device__ __forceinline__ void row_sum_chunk(const uint32_t (&pk)[16], float2& 
 __device__ __forceinline__ uint32_t p_col(int kc) { return static_cast<uint32_t>((kc >> 2) * 64 + (kc & 3) * 8); }
 
 // Buffer releases, made by lane 0 of the first softmax warp of the item's last query tile (nt-1)
-// right after it has seen the commit on s_full[nt-1] that follows S_{nt-1}(j). A commit tracks
+// once it has seen the commit on s_full[nt-1] that follows S_{nt-1}(j) (right after its own P
+// chunk-0 hand-over, which must not wait for them). A commit tracks
 // every UMMA issued before it and the issuer runs tile 0's UMMAs of a block before tile 1's, so
 // that commit covers every tile's S(j) and every tile's P.V(j-1), issued before S(j). Those are
 // the two readers of ring stage `stage` (V of the block before and K_j), which is therefore
@@ -513,21 +514,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Warp-uniform outcome: the tcgen05.ld/st below are .sync.aligned.
         ok = mbar_wait_warp(&sm.s_full[t], j & 1, abort, p.status);
         if (!ok) break;
-        if (releaser) release_after_s(sm, j, j == n_kv - 1);
         tc_fence_after();
         // Two 32-column chunks of this row's half of S; chunk 1 is loading while chunk 0 is
-        // exponentiated, and each chunk's P is handed to the issuer as soon as it is in TMEM.
+        // exponentiated, and each chunk's P is handed to the issuer as soon as it is in TMEM. The
+        // hand-over of chunk 0 waits for nothing else -- not for chunk 1's load (no UMMA touches
+        // those columns before chunk 1's own hand-over), nor for the releaser's arrivals, which
+        // come after it (a release can be late, never early): the tile's slowest warp sets when
+        // the issuer starts P.V, so nothing may sit in front of it (2697-2700 cycles per block
+        // against 2765-2770 with the release and the wait ahead of the hand-over).
         uint32_t ra[32], rb[32], pk0[16], pk1[16];
         tmem_ld_32x32b_x32(s_addr, ra);
         tmem_wait_ld(ra);
         tmem_ld_32x32b_x32(s_addr + 32, rb);
         exp_chunk(ra, pk0);
         tmem_st_32x32b_x16(s_addr, pk0);
-        tmem_wait_ld(rb);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.p_part[t][0]);
+        if (releaser) release_after_s(sm, j, j == n_kv - 1);
+        tmem_wait_ld(rb);
         exp_chunk(rb, pk1);
         tmem_st_32x32b_x16(s_addr + 16, pk1);
         tmem_wait_st();
@@ -578,7 +584,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // release after S(0) of the next item covers both (the last P.V of an item is issued before the
 // next item's S(0)). Block j needs exactly V_j and K_{j+1}, one stage, so the issuer waits once
 // per block instead of twice (separate K and V slots): 2776-2778 cycles per block against
-// 2881-2886 (CTA 0, clock64, bench loop), bit-identical output.
+// 2881-2886 (CTA 0, clock64, bench loop), bit-identical output; with the softmax's chunk-0
+// hand-over ahead of the release (see attend_kernel), 2697-2700.
 // Used when the CTA itself writes plain (not TMA-staged) output: the TMA-staged epilogue borrows
 // the Q buffers, which this form refills early.
 struct Item {
@@ -719,7 +726,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool last = (j == it.n_kv - 1);
         ok = stage_ready(st);
         if (!ok) break;
-        tc_fence_after();
         const uint32_t vslot = v_lo + (2 * (st % 2)) * kTile16;
         const int kslot = 2 * (st % 2) + 1;
 #pragma unroll
@@ -777,19 +783,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; ok && j < it.n_kv; ++j, ++s_seen) {
         ok = mbar_wait_warp(&sm.s_full[t], s_seen & 1, abort, p.status);
         if (!ok) break;
-        if (releaser) release_after_s(sm, item_g0 + j, j == it.n_kv - 1);
         tc_fence_after();
-        uint32_t ra[32], rb[32], pk0[16], pk1[16];
+        uint32_t ra[32], rb[32], pk0[16], pk1[16];  // same order as attend_kernel (hand-over first)
         tmem_ld_32x32b_x32(s_addr, ra);
         tmem_wait_ld(ra);
         tmem_ld_32x32b_x32(s_addr + 32, rb);
         exp_chunk(ra, pk0);
         tmem_st_32x32b_x16(s_addr, pk0);
-        tmem_wait_ld(rb);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sm.p_part[t][0]);
+        if (releaser) release_after_s(sm, item_g0 + j, j == it.n_kv - 1);
+        tmem_wait_ld(rb);
         exp_chunk(rb, pk1);
         tmem_st_32x32b_x16(s_addr + 16, pk1);
         tmem_wait_st();

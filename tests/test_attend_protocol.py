@@ -12,7 +12,8 @@ order and with the same completion indices as the CUDA code:
   block, on o_full[t];
 * 16 softmax warps: exp of S into P (two hand-over chunks), the row-sum exchange over a named
   barrier (double-buffered by item parity) and the epilogue read of O; one warp of the item's
-  last query tile releases stage b0 + j (and, at the last block, Q) as it sees S(j) complete.
+  last query tile releases stage b0 + j (and, at the last block, Q) once it has seen S(j)
+  complete, right after its own chunk-0 hand-over.
 
 The 'hardware' runs at random times: TMA copies land, UMMAs execute in issue order, commits
 arrive. mbarrier waits use the hardware's parity semantics (a wait for parity p returns once the
@@ -155,16 +156,16 @@ def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, release_from_tile0
             for j in range(n_kv):
                 yield ("wait", s_full[t], s_seen)
                 s_seen += 1
-                if releaser:
-                    kv_empty[(item_b0 + j) % 2].arrive()  # stage b0 + j: V_{j-1} (or the last V before) and K_j
-                    if j == n_kv - 1:
-                        q_empty.arrive()
                 if s_reg[t][quad][half] != ("S", it["w"], t, j):
                     raise ProtocolError(f"softmax read S {s_reg[t][quad][half]}, wanted {('S', it['w'], t, j)}")
                 for c in range(2):
                     yield ("step",)
                     p_reg[t][quad][half][c] = ("P", it["w"], t, j)
                     p_part[t][c].arrive()
+                    if c == 0 and releaser:  # after its own chunk-0 hand-over, as the kernel does
+                        kv_empty[(item_b0 + j) % 2].arrive()  # stage b0 + j: V_{j-1} (or the last V before) and K_j
+                        if j == n_kv - 1:
+                            q_empty.arrive()
             lb = n_done & 1
             l_part[lb][t][half][quad] = it["w"]
             gen = named[t][1]
