@@ -68,12 +68,12 @@ GRIDS = {"512": (32, 32), "1024": (64, 64), "2048": (128, 128)}
 # bytes; other configurations report null. A captured launch writes its outputs into L2, and the
 # part still dirty in L2 when it ends is written back during later launches, so an HBM-bound
 # kernel's figure can sit below its algorithmic bytes.
-NCU_TRAFFIC_BYTES = {"attend@1024": 89_999_616, "qk_prep@1024": 118_335_744, "w8a8_gemm@config4": 86_272_768}
+NCU_TRAFFIC_BYTES = {"attend@1024": 89_390_848, "qk_prep@1024": 118_335_744, "w8a8_gemm@config4": 86_272_768}
 NCU_TRAFFIC_NOTE = "ncu dram__bytes_read.sum + dram__bytes_write.sum of one captured launch at this workload"
 # The same counters with the cache left as the bench step leaves it (ncu --cache-control none,
 # application replay; mean of the launches of two timed steps): inside the step a kernel's window
 # also carries the write-back of what the kernel before it left dirty in L2.
-NCU_TRAFFIC_IN_STEP = {"attend@1024": 78_414_080, "qk_prep@1024": 157_494_144,
+NCU_TRAFFIC_IN_STEP = {"attend@1024": 78_609_152, "qk_prep@1024": 156_817_024,
                        "w8a8_gemm@config4": 109_930_368, "quantize_act@config4": 47_982_720}
 NCU_TRAFFIC_IN_STEP_NOTE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum inside the bench step "
                             "(--cache-control none, application replay), mean of two launches")
