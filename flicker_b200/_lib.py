@@ -43,6 +43,7 @@ SIGNATURES = {
     "flk_attend": (_int, [_u16p, _u16p, _u16p, _int, _int, _int, _int, _u16p, ctypes.c_void_p,
                           ctypes.c_size_t, ctypes.c_void_p]),
     "flk_attend_workspace_size": (ctypes.c_size_t, [_int, _int, _int, _int]),
+    "flk_attend_schedule": (_int, [_int, _int, _int, _int, _int, ctypes.POINTER(ctypes.c_longlong)]),
     "flk_attend_noalloc": (_int, [_u16p, _u16p, _u16p, _int, _int, _int, _int, _u16p, ctypes.c_void_p]),
     "flk_w8a8_quantize_act": (_int, [_u16p, _f32p, _int, _int, ctypes.c_void_p, _f32p, ctypes.c_void_p]),
     "flk_w8a8_gemm": (_int, [ctypes.c_void_p, ctypes.c_void_p, _f32p, _f32p, _int, _int, _int, _u16p,

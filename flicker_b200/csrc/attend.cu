@@ -42,6 +42,7 @@
 #include <mutex>
 
 #include "flicker_b200.h"
+#include "attend_schedule.cuh"
 #include "ptx.cuh"
 #include "quotient.cuh"
 
@@ -113,10 +114,17 @@ __device__ __forceinline__ void multimem_st16(void* addr, uint4 v) {
 struct Params {
   int S;          // sequence length (multiple of 128)
   int n_tiles;    // S / 128
-  int n_splits;   // KV splits; 1 = the CTA normalises and writes o itself
   int BH;         // batch x heads
   int n_pairs;    // (n_tiles + 1) / 2 query-tile pairs per (batch, head)
-  int n_items;    // BH * n_pairs * n_splits work items (persistent kernel)
+  // Work units (AttendSchedule): items [0, n_full) whole, then n_a items split s_a ways over KV,
+  // then the remaining items split s_b ways, split index fastest. A whole item's CTA normalises
+  // and writes o itself; a piece of a split item writes partials. n_units units in all.
+  int n_full, n_a, s_a, s_b;
+  int n_units;
+  // Partial rows: items split s_a ways own output rows [pa0, pa1), those split s_b ways
+  // [pa1, pb1); partial row (slot) of query row r in piece i: tier A (r - pa0) + i (pa1 - pa0),
+  // tier B s_a (pa1 - pa0) + (r - pa1) + i (pb1 - pa1).
+  long long pa0, pa1, pb1;
   OutLayout out;  // bf16 output
   // When a merged output goes to several buffers (a head-sharded call storing into its peers'
   // outputs) and the CTA writes o itself: one TMA map per buffer over [B*S, H_out*128] bf16,
@@ -127,10 +135,48 @@ struct Params {
   // multimem.st in whole 128-byte row pieces (8 lanes per row), which NVLink carries as full lines.
   int stage_mc;
   CUtensorMap out_maps[kMaxOuts];
-  float* acc;     // split > 1: [n_splits, B*H*S, 128] fp32 un-normalised partial P.V
-  float* lsum;    // split > 1: [n_splits, B*H*S] fp32 partial row sums
+  float* acc;     // split items: [partial rows, 128] fp32 un-normalised partial P.V
+  float* lsum;    // split items: [partial rows] fp32 partial row sums
   int* status;    // device status word
 };
+
+// One work unit: query tiles [t0, t0 + nt) of (batch, head) bh against KV blocks [kv0, kv0 + n_kv),
+// piece `split` of `splits` (splits == 1: a whole item). A piece's partial row for query row
+// `grow` is pbase + grow.
+struct Item {
+  int bh, t0, nt, split, splits, kv0, n_kv;
+  long long pbase;
+};
+
+__device__ __forceinline__ Item decode_item(const Params& p, int w) {
+  Item it;
+  int item;
+  if (w < p.n_full) {
+    item = w;
+    it.split = 0;
+    it.splits = 1;
+    it.pbase = 0;
+  } else if (w - p.n_full < p.n_a * p.s_a) {
+    const int u = w - p.n_full;
+    item = p.n_full + u / p.s_a;
+    it.split = u % p.s_a;
+    it.splits = p.s_a;
+    it.pbase = it.split * (p.pa1 - p.pa0) - p.pa0;
+  } else {
+    const int u = w - p.n_full - p.n_a * p.s_a;
+    item = p.n_full + p.n_a + u / p.s_b;
+    it.split = u % p.s_b;
+    it.splits = p.s_b;
+    it.pbase = p.s_a * (p.pa1 - p.pa0) + it.split * (p.pb1 - p.pa1) - p.pa1;
+  }
+  const int pair = item % p.n_pairs;
+  it.bh = item / p.n_pairs;
+  it.t0 = pair * 2;
+  it.nt = min(2, p.n_tiles - it.t0);
+  it.kv0 = static_cast<int>(static_cast<long long>(p.n_tiles) * it.split / it.splits);
+  it.n_kv = static_cast<int>(static_cast<long long>(p.n_tiles) * (it.split + 1) / it.splits) - it.kv0;
+  return it;
+}
 
 __device__ __forceinline__ Smem* smem_ptr(uint8_t* raw) {
   const uintptr_t a = (reinterpret_cast<uintptr_t>(raw) + 1023) & ~static_cast<uintptr_t>(1023);
@@ -266,13 +312,14 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int c0, int
 
 // Epilogue of one softmax warp: its 32 rows x 64 columns of O from TMEM, either normalised and
 // rounded to bf16 (o = bf16(acc / l), kernels.py:130, the quotient correctly rounded through one
-// reciprocal per row) or, for a KV split, the fp32 partials.
+// reciprocal per row) or, for a piece of a split item (splits > 1), the fp32 partials in partial
+// row pbase + grow.
 // Kept out of line so that this once-per-CTA code sits apart from the KV loop's code. `stage`
 // is this warp's 4 KB of shared memory (1024-byte aligned, free once the tile's MMAs are done).
-__device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t grow, int half, int split, float l,
-                                        uint8_t* stage) {
+__device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t grow, int half, int splits,
+                                        long long pbase, float l, uint8_t* stage) {
   const float rl = __frcp_rn(l);
-  if (p.n_splits == 1 && (p.tma_out || p.stage_mc)) {
+  if (splits == 1 && (p.tma_out || p.stage_mc)) {
     // Stage the 32 x 64 block in the 128-byte-swizzled layout the maps expect (16-byte unit j of
     // row r at position j ^ (r & 7): conflict-free), then one lane stores it to every buffer
     // (tma_out) or the warp stores it through the multicast address (stage_mc).
@@ -322,7 +369,7 @@ __device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t
       __threadfence_system();
     }
     __syncwarp();
-  } else if (p.n_splits == 1) {
+  } else if (splits == 1) {
     const size_t orow = out_row(grow, p.S, p.out) * kDim + half * 64;
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {
@@ -338,9 +385,9 @@ __device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t
     }
     if (p.out.n_out > 1 || p.out.multicast) __threadfence_system();
   } else {
-    // Partial result of this split: un-normalised fp32 accumulator and row sum.
-    const size_t plane = static_cast<size_t>(p.BH) * p.S;  // rows per split
-    float* arow = p.acc + (split * plane + grow) * kDim + half * 64;
+    // Partial result of this piece: un-normalised fp32 accumulator and row sum.
+    const size_t slot = static_cast<size_t>(pbase + static_cast<long long>(grow));
+    float* arow = p.acc + slot * kDim + half * 64;
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {
       uint32_t r[32];
@@ -350,7 +397,7 @@ __device__ __noinline__ void store_rows(const Params& p, uint32_t o_addr, size_t
 #pragma unroll
       for (int i = 0; i < 8; ++i) dst[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
     }
-    if (half == 0) p.lsum[split * plane + grow] = l;
+    if (half == 0) p.lsum[slot] = l;
   }
 }
 
@@ -363,13 +410,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
   const bool leader = lane == 0;  // the one lane of a converged warp that issues TMA / UMMA / commits
 
-  const int bh = blockIdx.y;
-  const int t0 = blockIdx.x * 2;
-  const int nt = min(2, p.n_tiles - t0);
-  // KV blocks [kv0, kv0 + n_kv) of this split. Without a running max the splits' (acc, l) simply add.
-  const int split = blockIdx.z;
-  const int kv0 = static_cast<int>(static_cast<long long>(p.n_tiles) * split / p.n_splits);
-  const int n_kv = static_cast<int>(static_cast<long long>(p.n_tiles) * (split + 1) / p.n_splits) - kv0;
+  // One work unit per CTA (blockIdx.x in the unit order of the schedule): query tiles [t0, t0 + nt)
+  // of (batch, head) bh against KV blocks [kv0, kv0 + n_kv). Without a running max the pieces'
+  // (acc, l) of a split item simply add.
+  const Item it = decode_item(p, blockIdx.x);
+  const int bh = it.bh, t0 = it.t0, nt = it.nt, kv0 = it.kv0, n_kv = it.n_kv;
   const int row_base = bh * p.S;
 
   if (threadIdx.x == 0) {
@@ -552,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t o_addr = tmem + lane_off + 256 + t * 128 + half * 64;
         const size_t grow = static_cast<size_t>(row_base) + (t0 + t) * kTile + row;  // global query row
-        store_rows(p, o_addr, grow, half, split, l, sm.q[t] + (sw % kSoftmaxWarps) * 4096);
+        store_rows(p, o_addr, grow, half, it.splits, it.pbase, l, sm.q[t] + (sw % kSoftmaxWarps) * 4096);
       }
     }
   }
@@ -566,9 +611,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------------------------------------
-// Persistent form: one CTA per SM walks work items w = blockIdx.x, blockIdx.x + gridDim.x, ...,
-// an item being what one CTA of attend_kernel does (two query tiles of one (batch, head), one KV
-// split). The barriers keep counting across items, so the next item's Q and K/V loads and its
+// Persistent form: one CTA per SM walks work units w = blockIdx.x, blockIdx.x + gridDim.x, ...,
+// a unit being what one CTA of attend_kernel does (two query tiles of one (batch, head), a whole
+// item or one piece of a split one). The barriers keep counting across items, so the next item's Q and K/V loads and its
 // first S = Q K^T run while the softmax warps are still in the current item's epilogue, instead
 // of after the CTA has exited and a new one has started, allocated TMEM and loaded its tiles.
 // Ordering across items, beyond that of attend_kernel:
@@ -588,23 +633,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 // hand-over ahead of the release (see attend_kernel), 2697-2700.
 // Used when the CTA itself writes plain (not TMA-staged) output: the TMA-staged epilogue borrows
 // the Q buffers, which this form refills early.
-struct Item {
-  int bh, t0, nt, split, kv0, n_kv;
-};
-
-__device__ __forceinline__ Item decode_item(const Params& p, int w) {
-  Item it;
-  it.split = w % p.n_splits;
-  const int rest = w / p.n_splits;
-  const int pair = rest % p.n_pairs;
-  it.bh = rest / p.n_pairs;
-  it.t0 = pair * 2;
-  it.nt = min(2, p.n_tiles - it.t0);
-  it.kv0 = static_cast<int>(static_cast<long long>(p.n_tiles) * it.split / p.n_splits);
-  it.n_kv = static_cast<int>(static_cast<long long>(p.n_tiles) * (it.split + 1) / p.n_splits) - it.kv0;
-  return it;
-}
-
 __global__ void __launch_bounds__(kThreads, 1)
     attend_persistent_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                              const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ Params p) {
@@ -662,7 +690,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       return issue_kv_stage(sm, &tm_k, &tm_v, G, v_row, k_row, leader, abort, p.status);
     };
     int pending_v = -1;  // row of the previous item's last V, loaded with this item's first K
-    for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x) {
+    for (int w = blockIdx.x; ok && w < p.n_units; w += gridDim.x) {
       const Item it = decode_item(p, w);
       const int row_base = it.bh * p.S;
       ok = issue_stage(pending_v, row_base + it.kv0 * kTile);
@@ -708,7 +736,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t blocks[2] = {0, 0};    // KV blocks done per tile: p_part phases consumed
     auto stage_ready = [&](uint32_t G) { return wait(&sm.kv_full[G % 2], (G / 2) & 1); };
     bool ok = true;
-    for (int w = blockIdx.x; ok && w < p.n_items; w += gridDim.x) {
+    for (int w = blockIdx.x; ok && w < p.n_units; w += gridDim.x) {
       const Item it = decode_item(p, w);
       // stage b0 (this item's first K) was waited for with the previous item's last V
       ok = wait(&sm.q_full, items & 1) && (b0 > 0 || stage_ready(0));
@@ -773,7 +801,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Once a wait has failed the warp does no more work, but it still meets its tile's named
     // barrier once per item, as its partner warps (which may not have seen the failure yet) do.
     bool ok = true;
-    for (int w = blockIdx.x; w < p.n_items; w += gridDim.x) {
+    for (int w = blockIdx.x; w < p.n_units; w += gridDim.x) {
       const Item it = decode_item(p, w);
       const uint32_t item_g0 = g0;
       g0 += it.n_kv;
@@ -815,7 +843,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) {
         tc_fence_after();
         const size_t grow = static_cast<size_t>(it.bh) * p.S + (it.t0 + t) * kTile + row;
-        store_rows(p, o_addr, grow, half, it.split, l, nullptr);
+        store_rows(p, o_addr, grow, half, it.splits, it.pbase, l, nullptr);
       }
     }
   }
@@ -828,28 +856,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// o = bf16(sum_s acc_s / sum_s l_s) over the KV splits; one thread per 8 output columns.
+// o = bf16(sum_i acc_i / sum_i l_i) over the pieces of the split items; one thread per 8 output
+// columns of query rows [pa0, pb1) (rows [pa0, pa1) split s_a ways, [pa1, pb1) s_b ways), the
+// pieces added in order.
+struct CombineParams {
+  long long pa0, pa1, pb1;
+  int s_a, s_b, S;
+};
 __global__ void __launch_bounds__(256) combine_splits_kernel(const float* __restrict__ acc,
-                                                             const float* __restrict__ lsum, int n_splits,
-                                                             long long rows, int S, const __grid_constant__ OutLayout L) {
+                                                             const float* __restrict__ lsum,
+                                                             const __grid_constant__ CombineParams c,
+                                                             const __grid_constant__ OutLayout L) {
   const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= rows * (kDim / 8)) return;
-  const long long row = idx / (kDim / 8);
+  if (idx >= (c.pb1 - c.pa0) * (kDim / 8)) return;
+  const long long row = c.pa0 + idx / (kDim / 8);
   const int col = static_cast<int>(idx % (kDim / 8)) * 8;
+  const bool tier_a = row < c.pa1;
+  const int n = tier_a ? c.s_a : c.s_b;
+  const long long first = tier_a ? row - c.pa0 : c.s_a * (c.pa1 - c.pa0) + (row - c.pa1);
+  const long long stride = tier_a ? c.pa1 - c.pa0 : c.pb1 - c.pa1;
   float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float l = 0.f;
-  for (int s = 0; s < n_splits; ++s) {
-    const float4* src = reinterpret_cast<const float4*>(acc + (s * rows + row) * kDim + col);
+  for (int s = 0; s < n; ++s) {
+    const long long slot = first + s * stride;
+    const float4* src = reinterpret_cast<const float4*>(acc + slot * kDim + col);
     const float4 x = src[0], y = src[1];
     a[0] += x.x; a[1] += x.y; a[2] += x.z; a[3] += x.w;
     a[4] += y.x; a[5] += y.y; a[6] += y.z; a[7] += y.w;
-    l += lsum[s * rows + row];
+    l += lsum[slot];
   }
   uint32_t pk[4];
   const float rl = __frcp_rn(l);
 #pragma unroll
   for (int i = 0; i < 4; ++i) pk[i] = pack_bf16x2(quotient_rn(a[2 * i], l, rl), quotient_rn(a[2 * i + 1], l, rl));
-  const size_t off = out_row(row, S, L) * kDim + col;
+  const size_t off = out_row(row, c.S, L) * kDim + col;
   if (L.multicast) {
     multimem_st16(L.o[0] + off, make_uint4(pk[0], pk[1], pk[2], pk[3]));
   } else {
@@ -929,23 +969,107 @@ static bool make_out_map(CUtensorMap* map, const void* base, long long rows, int
 static size_t attend_smem_bytes() { return sizeof(Smem) + 1024; }
 static_assert(sizeof(Smem) + 1024 <= 232448, "attend shared memory exceeds the 227 KB opt-in limit");
 
-// KV splits for a shape on a device with `sms` SMs: enough CTAs to fill one wave of SMs
-// when (batch x heads x query-tile pairs) alone would leave most of them idle.
-int attend_splits(int B, int H, int S, int sms) {
-  const long long ctas = static_cast<long long>(B) * H * ((S / kTile + 1) / 2);
-  if (ctas <= 0 || ctas * 2 > sms) return 1;
-  const int n_kv = S / kTile;
-  return static_cast<int>(std::min<long long>(n_kv, std::max<long long>(1, sms / ctas)));
+// First output row of item `item` (items are numbered (batch * H + head) * n_pairs + pair, each
+// covering 256 consecutive query rows, or 128 for the odd last tile of a (batch, head)).
+static long long item_row(int item, int n_pairs, int S) {
+  return static_cast<long long>(item / n_pairs) * S + static_cast<long long>(item % n_pairs) * 2 * kTile;
 }
 
-size_t attend_workspace_bytes(int B, int H, int S, int splits) {
-  if (splits <= 1) return 0;
-  const size_t rows = static_cast<size_t>(B) * H * S;
-  return splits * rows * (kDim + 1) * sizeof(float);
+AttendSchedule attend_unsplit(int B, int H, int S) {
+  AttendSchedule sch;
+  sch.n_items = static_cast<int>(std::min<long long>(INT32_MAX, static_cast<long long>(B) * H * ((S / kTile + 1) / 2)));
+  sch.n_full = sch.n_items;
+  return sch;
+}
+
+size_t attend_workspace_bytes(int B, int H, int S, const AttendSchedule& sch) {
+  if (!sch.split()) return 0;
+  const int n_pairs = (S / kTile + 1) / 2;
+  const long long pa0 = item_row(sch.n_full, n_pairs, S), pa1 = item_row(sch.n_full + sch.n_a, n_pairs, S);
+  const long long pb1 = static_cast<long long>(B) * H * S;
+  const long long slots = sch.s_a * (pa1 - pa0) + sch.s_b * (pb1 - pa1);
+  return static_cast<size_t>(slots) * (kDim + 1) * sizeof(float);
+}
+
+namespace {
+
+// Estimated cost of a schedule, in units of one 128-row KV block of one work unit (~2700 SM
+// cycles): the busiest CTA's blocks when unit u runs on CTA u % sms (the persistent kernel's
+// order; the one-unit-per-CTA kernel is dispatched in the same order), plus a fixed cost per unit
+// (its first S before any overlap, its epilogue) and per call (launch, ramp-up, drain), plus the
+// combine pass: a launch and the partials' traffic at ~9.75 MB of HBM per block time.
+constexpr double kUnitBlocks = 0.5, kCallBlocks = 7.0, kCombineBlocks = 2.0, kBytesPerBlock = 9.75e6;
+
+double schedule_cost(const AttendSchedule& sch, int B, int H, int S, int sms) {
+  const int n_tiles = S / kTile;
+  const long long F = sch.n_full, A = static_cast<long long>(sch.n_a) * sch.s_a, U = sch.units();
+  const double size_f = n_tiles + kUnitBlocks;
+  const double size_a = (n_tiles + sch.s_a - 1) / sch.s_a + kUnitBlocks;
+  const double size_b = (n_tiles + sch.s_b - 1) / sch.s_b + kUnitBlocks;
+  // number of units u in [lo, hi) with u % sms == c
+  auto count = [&](long long lo, long long hi, int c) -> long long {
+    auto upto = [&](long long n) { return n <= c ? 0 : (n - 1 - c) / sms + 1; };  // u in [0, n)
+    return hi > lo ? upto(hi) - upto(lo) : 0;
+  };
+  double worst = 0.0;
+  for (int c = 0; c < sms && c < U; ++c)
+    worst = std::max(worst, count(0, F, c) * size_f + count(F, F + A, c) * size_a + count(F + A, U, c) * size_b);
+  double cost = worst + kCallBlocks;
+  if (sch.split()) {
+    const double slots = static_cast<double>(attend_workspace_bytes(B, H, S, sch)) / ((kDim + 1) * sizeof(float));
+    const double rows = static_cast<double>(B) * H * S - item_row(sch.n_full, (n_tiles + 1) / 2, S);
+    // partial rows written (half of it hidden under the attention) and read back, bf16 rows out
+    cost += kCombineBlocks + (slots * (kDim + 1) * 4 * 1.5 + rows * kDim * 2) / kBytesPerBlock;
+  }
+  return cost;
+}
+
+}  // namespace
+
+// The schedule for a shape on a device with `sms` SMs.
+// Base rule: every item whole, unless (batch x heads x query-tile pairs) would fill at most half
+// of the SMs; then every item is split evenly, into enough pieces to fill one wave.
+// Tiered rule: the items that fill whole waves stay whole; of the rest, n_a are split s_a ways
+// (at most one piece per SM) and the others s_b <= 16 ways (at most one more piece per SM), so the last
+// wave is cut into pieces that end together instead of leaving SMs idle (216 items on 148 SMs:
+// 36 + 18 blocks on the busiest SM instead of 2 x 36). Taken when its estimated cost is at least
+// 5 % below the base rule's.
+AttendSchedule attend_schedule(int B, int H, int S, int sms) {
+  AttendSchedule base = attend_unsplit(B, H, S);
+  const int n_tiles = S / kTile;
+  const long long items = base.n_items;
+  if (items <= 0 || sms <= 0 || n_tiles <= 0) return base;
+  if (items * 2 <= sms) {
+    const int s = static_cast<int>(std::min<long long>(n_tiles, std::max<long long>(1, sms / items)));
+    if (s > 1) {
+      base.n_full = 0;
+      base.n_a = base.n_items;
+      base.s_a = base.s_b = s;
+    }
+  }
+  AttendSchedule best = base;
+  const double base_cost = schedule_cost(base, B, H, S, sms);
+  double best_cost = base_cost;
+  const long long whole = (items / sms) * sms;  // items filling whole waves
+  const long long rest = items - whole;
+  for (int s_a = 2; rest > 0 && s_a <= std::min(n_tiles, 8); ++s_a) {
+    AttendSchedule c;
+    c.n_items = base.n_items;
+    c.n_full = static_cast<int>(whole);
+    c.n_a = static_cast<int>(std::min<long long>(rest, sms / s_a));
+    c.s_a = s_a;
+    const long long rb = rest - c.n_a;
+    c.s_b = rb > 0 ? static_cast<int>(std::min<long long>({n_tiles, sms / rb, 16})) : s_a;
+    if (c.n_a == 0 || c.s_b < 2 || c.units() > INT32_MAX) continue;
+    const double cost = schedule_cost(c, B, H, S, sms);
+    if (cost < best_cost) best = c, best_cost = cost;
+  }
+  return best_cost < 0.95 * base_cost ? best : base;
 }
 
 int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S,
-                      const OutLayout& out, int splits, void* workspace, int* status, cudaStream_t stream) {
+                      const OutLayout& out, const AttendSchedule& sch, void* workspace, int* status,
+                      cudaStream_t stream) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return FLK_ERR_CUDA;
   if (dev < 0 || dev >= 64) return FLK_ERR_UNSUPPORTED;
@@ -971,10 +1095,11 @@ int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
     sms = sm_count[dev];
   }
   const long long rows = static_cast<long long>(B) * H * S;
-  // Gathering calls that write o themselves stage each warp's block in shared memory (the Q
-  // buffers, free once the item's UMMAs are done) and store it as whole rows: by TMA into every
-  // buffer, or by multimem stores through a multicast address.
-  const bool staged = out.merged && (out.n_out > 1 || out.multicast) && splits == 1;
+  // Gathering calls in which CTAs write o themselves (some items whole) stage each warp's block
+  // in shared memory (the Q buffers, free once the item's UMMAs are done) and store it as whole
+  // rows: by TMA into every buffer, or by multimem stores through a multicast address. They run
+  // one unit per CTA; the pieces of split items write partials there as in the persistent form.
+  const bool staged = out.merged && (out.n_out > 1 || out.multicast) && sch.n_full > 0;
   const bool tma_out = staged && !out.multicast;
   const bool persistent = !staged;
   CUtensorMap mq, mk, mv;
@@ -983,12 +1108,18 @@ int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
   Params p;
   p.S = S;
   p.n_tiles = S / kTile;
-  p.n_splits = splits;
   p.BH = B * H;
   p.n_pairs = (p.n_tiles + 1) / 2;
-  const long long items = static_cast<long long>(p.BH) * p.n_pairs * splits;
-  if (items > INT32_MAX) return FLK_ERR_UNSUPPORTED;
-  p.n_items = static_cast<int>(items);
+  const long long units = sch.units();
+  if (sch.n_items != static_cast<long long>(p.BH) * p.n_pairs || units > INT32_MAX) return FLK_ERR_UNSUPPORTED;
+  p.n_full = sch.n_full;
+  p.n_a = sch.n_a;
+  p.s_a = sch.s_a;
+  p.s_b = sch.s_b;
+  p.n_units = static_cast<int>(units);
+  p.pa0 = item_row(sch.n_full, p.n_pairs, S);
+  p.pa1 = item_row(sch.n_full + sch.n_a, p.n_pairs, S);
+  p.pb1 = rows;
   p.out = out;
   p.tma_out = tma_out ? 1 : 0;
   p.stage_mc = (staged && out.multicast) ? 1 : 0;
@@ -996,12 +1127,12 @@ int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
     for (int d = 0; d < out.n_out; ++d)
       if (!make_out_map(&p.out_maps[d], out.o[d], static_cast<long long>(B) * S, out.H_out * kDim))
         return FLK_ERR_CUDA;
-  p.acc = splits > 1 ? static_cast<float*>(workspace) : nullptr;
-  p.lsum = splits > 1 ? p.acc + static_cast<size_t>(splits) * rows * kDim : nullptr;
+  const size_t slots = attend_workspace_bytes(B, H, S, sch) / ((kDim + 1) * sizeof(float));
+  p.acc = sch.split() ? static_cast<float*>(workspace) : nullptr;
+  p.lsum = sch.split() ? p.acc + slots * kDim : nullptr;
   p.status = status;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = persistent ? dim3(static_cast<unsigned>(std::min<long long>(items, sms)))
-                           : dim3(p.n_pairs, p.BH, splits);
+  cfg.gridDim = dim3(static_cast<unsigned>(persistent ? std::min<long long>(units, sms) : units));
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = attend_smem_bytes();
   cfg.stream = stream;
@@ -1014,17 +1145,18 @@ int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
       cudaSuccess)
     return FLK_ERR_CUDA;
   if (cudaGetLastError() != cudaSuccess) return FLK_ERR_CUDA;
-  if (splits > 1) {
-    const long long threads = rows * (kDim / 8);
-    combine_splits_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(
-        p.acc, p.lsum, splits, rows, S, out);
+  if (sch.split()) {
+    const CombineParams c{p.pa0, p.pa1, p.pb1, p.s_a, p.s_b, S};
+    const long long threads = (p.pb1 - p.pa0) * (kDim / 8);
+    combine_splits_kernel<<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(p.acc, p.lsum, c, out);
     if (cudaGetLastError() != cudaSuccess) return FLK_ERR_CUDA;
   }
   return FLK_OK;
 }
 
 int launch_attend_layout(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, uint16_t* o,
-                         int merged, int splits, void* workspace, int* status, cudaStream_t stream) {
+                         int merged, const AttendSchedule& sch, void* workspace, int* status,
+                         cudaStream_t stream) {
   OutLayout out{};
   out.merged = merged;
   out.H = H;
@@ -1032,14 +1164,14 @@ int launch_attend_layout(const uint16_t* q, const uint16_t* k, const uint16_t* v
   out.h0 = 0;
   out.n_out = 1;
   out.o[0] = o;
-  return launch_attend_out(q, k, v, B, H, S, out, splits, workspace, status, stream);
+  return launch_attend_out(q, k, v, B, H, S, out, sch, workspace, status, stream);
 }
 
 // Merged rows of H_out heads, this call's heads at [h0, h0 + H), written into each of the
 // n_out buffers (this GPU's and peers' memory, all addressable from this device).
 int launch_attend_gather(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S,
-                         uint16_t* const* outs, int n_out, int H_out, int h0, int splits, void* workspace,
-                         int* status, cudaStream_t stream) {
+                         uint16_t* const* outs, int n_out, int H_out, int h0, const AttendSchedule& sch,
+                         void* workspace, int* status, cudaStream_t stream) {
   if (n_out < 1 || n_out > kMaxOuts) return FLK_ERR_INVALID_ARGUMENT;
   OutLayout out{};
   out.merged = 1;
@@ -1048,14 +1180,14 @@ int launch_attend_gather(const uint16_t* q, const uint16_t* k, const uint16_t* v
   out.h0 = h0;
   out.n_out = n_out;
   for (int d = 0; d < n_out; ++d) out.o[d] = outs[d];
-  return launch_attend_out(q, k, v, B, H, S, out, splits, workspace, status, stream);
+  return launch_attend_out(q, k, v, B, H, S, out, sch, workspace, status, stream);
 }
 
 // Merged rows of H_out heads, this call's heads at [h0, h0 + H), stored once through the
 // multicast address `out_mc`, which the NVSwitch replicates into every bound rank's buffer.
 int launch_attend_gather_multicast(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S,
-                                   uint16_t* out_mc, int H_out, int h0, int splits, void* workspace, int* status,
-                                   cudaStream_t stream) {
+                                   uint16_t* out_mc, int H_out, int h0, const AttendSchedule& sch,
+                                   void* workspace, int* status, cudaStream_t stream) {
   OutLayout out{};
   out.merged = 1;
   out.H = H;
@@ -1064,7 +1196,7 @@ int launch_attend_gather_multicast(const uint16_t* q, const uint16_t* k, const u
   out.n_out = 1;
   out.multicast = 1;
   out.o[0] = out_mc;
-  return launch_attend_out(q, k, v, B, H, S, out, splits, workspace, status, stream);
+  return launch_attend_out(q, k, v, B, H, S, out, sch, workspace, status, stream);
 }
 
 int attend_binary_version(int* version) {
@@ -1076,8 +1208,8 @@ int attend_binary_version(int* version) {
 
 // Head-major output ([B, H, S, 128]), the layout of kernels.attend.
 int launch_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, uint16_t* o,
-                  int splits, void* workspace, int* status, cudaStream_t stream) {
-  return launch_attend_layout(q, k, v, B, H, S, o, 0, splits, workspace, status, stream);
+                  const AttendSchedule& sch, void* workspace, int* status, cudaStream_t stream) {
+  return launch_attend_layout(q, k, v, B, H, S, o, 0, sch, workspace, status, stream);
 }
 
 }  // namespace flk

@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <mutex>
 
+#include "attend_schedule.cuh"
 #include "flicker_b200.h"
 
 namespace flk {
@@ -17,21 +18,19 @@ int launch_qk_prep(const uint16_t* qkv, const uint16_t* q_scale, const uint16_t*
                    const float* sin_t, float q_gain, int B, int L, int H, int S_out, int row0, uint16_t* q,
                    uint16_t* k, uint16_t* v, cudaStream_t stream);
 int launch_attend_layout(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, uint16_t* o,
-                         int merged, int splits, void* workspace, int* status, cudaStream_t stream);
+                         int merged, const AttendSchedule& sch, void* workspace, int* status, cudaStream_t stream);
 int launch_attend_gather(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S,
-                         uint16_t* const* outs, int n_out, int H_out, int h0, int splits, void* workspace,
-                         int* status, cudaStream_t stream);
+                         uint16_t* const* outs, int n_out, int H_out, int h0, const AttendSchedule& sch,
+                         void* workspace, int* status, cudaStream_t stream);
 int launch_attend_gather_multicast(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S,
-                                   uint16_t* out_mc, int H_out, int h0, int splits, void* workspace, int* status,
-                                   cudaStream_t stream);
-int attend_splits(int B, int H, int S, int sms);
+                                   uint16_t* out_mc, int H_out, int h0, const AttendSchedule& sch,
+                                   void* workspace, int* status, cudaStream_t stream);
 int launch_linear_bf16(const uint16_t* x, const uint16_t* wt, int M, int N, int K, uint16_t* y, int* status, int sms,
                        cudaStream_t stream);
 int launch_linear_qk_prep(const uint16_t* x, const uint16_t* wt, int M, int N, int K, int L, int H,
                           const uint16_t* q_scale, const uint16_t* k_scale, const float* cos_t, const float* sin_t,
                           float q_gain, uint16_t* q, uint16_t* k, uint16_t* v, int S_out, int row0, uint16_t* rest,
                           int* status, int sms, cudaStream_t stream);
-size_t attend_workspace_bytes(int B, int H, int S, int splits);
 int launch_w8a8_gemm(const int8_t* xq, const int8_t* wq, const float* x_scale, const float* w_scale, int M, int N,
                      int K, uint16_t* y, int32_t* acc_out, int* status, int sms, cudaStream_t stream);
 int launch_quantize_act(const uint16_t* x, const float* inv_s, int M, int K, int8_t* xq, float* x_scale,
@@ -172,12 +171,38 @@ int flk_qk_prep_into(const uint16_t* qkv, const uint16_t* q_scale, const uint16_
   return qk_prep_entry(qkv, q_scale, k_scale, cos, sin, q_gain, B, L, H, D, q, k, v, S_out, row0, stream);
 }
 
+// The schedule of an attention call: low-occupancy shapes, and shapes whose last wave of work
+// items would leave SMs idle, run (partly) split over KV when the caller provides the workspace
+// the schedule needs; a caller that passes no workspace (NULL, 0 bytes) gets every item whole.
+static int pick_schedule(int B, int H, int S, int sms, void* workspace, size_t ws_bytes,
+                         flk::AttendSchedule* sch) {
+  *sch = flk::attend_schedule(B, H, S, sms);
+  if (!sch->split()) return FLK_OK;
+  if (workspace == nullptr && ws_bytes == 0) {
+    *sch = flk::attend_unsplit(B, H, S);
+    return FLK_OK;
+  }
+  if (workspace == nullptr || ws_bytes < flk::attend_workspace_bytes(B, H, S, *sch) || !aligned16(workspace))
+    return FLK_ERR_WORKSPACE;
+  return FLK_OK;
+}
+
 size_t flk_attend_workspace_size(int B, int H, int S, int D) {
   int err = FLK_OK;
   if (!attend_shape_ok(B, H, S, D, &err) || static_cast<long long>(B) * S == 0) return 0;
   const DeviceState* st = device_state(&err);
   if (!st) return 0;
-  return flk::attend_workspace_bytes(B, H, S, flk::attend_splits(B, H, S, st->sms));
+  return flk::attend_workspace_bytes(B, H, S, flk::attend_schedule(B, H, S, st->sms));
+}
+
+int flk_attend_schedule(int B, int H, int S, int D, int sms, long long* out) {
+  int err = FLK_OK;
+  if (!attend_shape_ok(B, H, S, D, &err)) return err;
+  if (out == nullptr || sms <= 0) return FLK_ERR_INVALID_ARGUMENT;
+  const flk::AttendSchedule sch = flk::attend_schedule(B, H, S, sms);
+  const long long v[6] = {sch.n_items, sch.n_full, sch.n_a, sch.s_a, sch.s_b, sch.units()};
+  for (int i = 0; i < 6; ++i) out[i] = v[i];
+  return FLK_OK;
 }
 
 static int attend_entry(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, int D,
@@ -190,18 +215,9 @@ static int attend_entry(const uint16_t* q, const uint16_t* k, const uint16_t* v,
     if (p == nullptr || !aligned16(p)) return FLK_ERR_INVALID_ARGUMENT;
   const DeviceState* st = device_state(&err);
   if (!st) return err;
-  // Low-occupancy shapes run split over KV when the caller provides the workspace; a caller
-  // that passes no workspace (NULL, 0 bytes) gets the unsplit kernel.
-  int splits = flk::attend_splits(B, H, S, st->sms);
-  if (splits > 1) {
-    const size_t need = flk::attend_workspace_bytes(B, H, S, splits);
-    if (workspace == nullptr && ws_bytes == 0) {
-      splits = 1;
-    } else if (workspace == nullptr || ws_bytes < need || !aligned16(workspace)) {
-      return FLK_ERR_WORKSPACE;
-    }
-  }
-  return flk::launch_attend_layout(q, k, v, B, H, S, o, merged, splits, workspace, st->status,
+  flk::AttendSchedule sch;
+  if (const int rc = pick_schedule(B, H, S, st->sms, workspace, ws_bytes, &sch); rc != FLK_OK) return rc;
+  return flk::launch_attend_layout(q, k, v, B, H, S, o, merged, sch, workspace, st->status,
                                    static_cast<cudaStream_t>(stream));
 }
 
@@ -230,16 +246,9 @@ int flk_attend_gather(const uint16_t* q, const uint16_t* k, const uint16_t* v, i
     if (outs[d] == nullptr || !aligned16(outs[d])) return FLK_ERR_INVALID_ARGUMENT;
   const DeviceState* st = device_state(&err);
   if (!st) return err;
-  int splits = flk::attend_splits(B, H, S, st->sms);
-  if (splits > 1) {
-    const size_t need = flk::attend_workspace_bytes(B, H, S, splits);
-    if (workspace == nullptr && ws_bytes == 0) {
-      splits = 1;
-    } else if (workspace == nullptr || ws_bytes < need || !aligned16(workspace)) {
-      return FLK_ERR_WORKSPACE;
-    }
-  }
-  return flk::launch_attend_gather(q, k, v, B, H, S, outs, n_outs, H_total, h0, splits, workspace, st->status,
+  flk::AttendSchedule sch;
+  if (const int rc = pick_schedule(B, H, S, st->sms, workspace, ws_bytes, &sch); rc != FLK_OK) return rc;
+  return flk::launch_attend_gather(q, k, v, B, H, S, outs, n_outs, H_total, h0, sch, workspace, st->status,
                                    static_cast<cudaStream_t>(stream));
 }
 
@@ -255,16 +264,9 @@ int flk_attend_gather_multicast(const uint16_t* q, const uint16_t* k, const uint
     if (p == nullptr || !aligned16(p)) return FLK_ERR_INVALID_ARGUMENT;
   const DeviceState* st = device_state(&err);
   if (!st) return err;
-  int splits = flk::attend_splits(B, H, S, st->sms);
-  if (splits > 1) {
-    const size_t need = flk::attend_workspace_bytes(B, H, S, splits);
-    if (workspace == nullptr && ws_bytes == 0) {
-      splits = 1;
-    } else if (workspace == nullptr || ws_bytes < need || !aligned16(workspace)) {
-      return FLK_ERR_WORKSPACE;
-    }
-  }
-  return flk::launch_attend_gather_multicast(q, k, v, B, H, S, out_mc, H_total, h0, splits, workspace, st->status,
+  flk::AttendSchedule sch;
+  if (const int rc = pick_schedule(B, H, S, st->sms, workspace, ws_bytes, &sch); rc != FLK_OK) return rc;
+  return flk::launch_attend_gather_multicast(q, k, v, B, H, S, out_mc, H_total, h0, sch, workspace, st->status,
                                              static_cast<cudaStream_t>(stream));
 }
 

@@ -5,13 +5,14 @@
 // without a scratch buffer: the runtime owns all device memory, and calling cudaMalloc from
 // inside the handler would synchronise the device in the middle of XLA's asynchronous stream
 // work. A serving loop that must never stall on a device-wide allocation is in the same spot.
-// flk_attend asks such callers for a workspace when a shape runs split over KV; this entry
-// point instead uses a fixed scratch array compiled into the library, so it allocates nothing.
+// flk_attend asks such callers for a workspace when a shape runs (partly) split over KV; this
+// entry point instead uses a fixed scratch array compiled into the library, so it allocates
+// nothing.
 //
-// The scratch is a file-scope __device__ array of kScratchBytes (16 MiB). Every GPU that loads
+// The scratch is a file-scope __device__ array of kScratchBytes (32 MiB). Every GPU that loads
 // this library holds it until the process exits, whether or not this entry point is called.
-// Shapes whose split needs more than that are refused with FLK_ERR_WORKSPACE; shapes that do
-// not split (most large ones) never touch it.
+// Shapes whose schedule needs more than that are refused with FLK_ERR_WORKSPACE; shapes that do
+// not split (the large, evenly filled ones) never touch it.
 //
 // Set-up: the first call on a device, with that device current, looks up the array's device
 // address with cudaGetSymbolAddress and caches it per device. (A host-side reference to the
@@ -19,27 +20,26 @@
 // Make that first call before any stream capture on the device.
 //
 // Sharing: all calls share the one array, and it keeps whatever the last call wrote. Nothing in
-// it has to start at zero: every KV split writes all of its partial rows before the combine
-// kernel reads them. Two calls whose kernels overlap on the GPU (e.g. on different streams
+// it has to start at zero: every piece of a split item writes all of its partial rows before the
+// combine kernel reads them. Two calls whose kernels overlap on the GPU (e.g. on different streams
 // without ordering between them) race on the array; callers must order them.
 #include <cuda_runtime.h>
 
 #include <cstdint>
 #include <mutex>
 
+#include "attend_schedule.cuh"
 #include "flicker_b200.h"
 
 namespace flk {
 int launch_attend(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S, uint16_t* o,
-                  int splits, void* workspace, int* status, cudaStream_t stream);
-int attend_splits(int B, int H, int S, int sms);
-size_t attend_workspace_bytes(int B, int H, int S, int splits);
+                  const AttendSchedule& sch, void* workspace, int* status, cudaStream_t stream);
 int* current_device_status(int* err);
 }  // namespace flk
 
 namespace {
 
-constexpr size_t kScratchBytes = size_t(16) << 20;  // 16 MiB
+constexpr size_t kScratchBytes = size_t(32) << 20;  // 32 MiB
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
@@ -108,10 +108,10 @@ extern "C" int flk_attend_noalloc(const uint16_t* q, const uint16_t* k, const ui
   int err = FLK_OK;
   const NoAllocDevice* st = noalloc_device(&err);
   if (!st) return err;
-  const int splits = flk::attend_splits(B, H, S, st->sms);
-  if (flk::attend_workspace_bytes(B, H, S, splits) > kScratchBytes) return FLK_ERR_WORKSPACE;
+  const flk::AttendSchedule sch = flk::attend_schedule(B, H, S, st->sms);
+  if (flk::attend_workspace_bytes(B, H, S, sch) > kScratchBytes) return FLK_ERR_WORKSPACE;
   int* status = flk::current_device_status(&err);  // the library's device status word
   if (!status) return err;
-  return flk::launch_attend(q, k, v, B, H, S, o, splits, splits > 1 ? st->scratch : nullptr, status,
+  return flk::launch_attend(q, k, v, B, H, S, o, sch, sch.split() ? st->scratch : nullptr, status,
                             static_cast<cudaStream_t>(stream));
 }

@@ -121,13 +121,23 @@ int flk_attend_gather_multicast(const uint16_t* q, const uint16_t* k, const uint
 size_t flk_attend_workspace_size(int B, int H, int S, int D);
 
 /*
+ * How flk_attend (given its workspace) cuts the work of a B x H x S call over a device with `sms`
+ * SMs. No counterpart in the reference (Pallas picks its grid itself); a host-only query for
+ * tests and capacity planning, no GPU work. A work item is two 128-row query tiles of one
+ * (batch, head); out[0..5] receive: items, items kept whole (the first ones), items split s_a
+ * ways, s_a, s_b (the remaining items' split count) and work units. Returns FLK_OK or
+ * FLK_ERR_INVALID_ARGUMENT / FLK_ERR_UNSUPPORTED for shapes flk_attend refuses.
+ */
+int flk_attend_schedule(int B, int H, int S, int D, int sms, long long* out);
+
+/*
  * flk_attend for callers that cannot allocate device memory. No counterpart in the reference.
  * Same arguments as flk_attend minus the workspace, and the same result as flk_attend given the
- * workspace it asks for: when the shape runs split over KV, the partial results go to a 16 MiB
- * scratch array built into the library (held on every GPU that loads it) instead of caller
- * memory, so the call allocates nothing. Shapes whose split needs more than 16 MiB of scratch
- * (e.g. B=1, H=2, S=8192 on a 148-SM B200) return FLK_ERR_WORKSPACE, although flk_attend with
- * no workspace (NULL, 0) runs them unsplit: this entry point never silently changes the split.
+ * workspace it asks for: when the shape runs (partly) split over KV, the partial results go to a
+ * 32 MiB scratch array built into the library (held on every GPU that loads it) instead of caller
+ * memory, so the call allocates nothing. Shapes whose schedule needs more than 32 MiB of scratch
+ * (e.g. B=1, H=6, S=16896 on a 148-SM B200) return FLK_ERR_WORKSPACE, although flk_attend with
+ * no workspace (NULL, 0) runs them unsplit: this entry point never silently changes the schedule.
  * The first call on a device sets up the scratch address (make it before any stream capture);
  * calls share the scratch, so calls whose kernels overlap on the GPU race and must be ordered
  * by the caller.

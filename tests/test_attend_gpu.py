@@ -161,11 +161,62 @@ def test_split_kv_matches_unsplit(b, h, s):
     assert fb.device_status() == 0
 
 
+def device_schedule(b, h, s):
+    """flk_attend_schedule on this device's SM count: (items, whole, split s_a ways, s_a, s_b, units)."""
+    import ctypes
+
+    from flicker_b200 import _lib
+
+    out = (ctypes.c_longlong * 6)()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert _lib.lib().flk_attend_schedule(b, h, s, 128, sms, out) == 0
+    return tuple(out)
+
+
+# 216 items (12 heads at S=4608) on 148 SMs: one wave whole, the last 68 items in halves; 234 items
+# (13 heads): one wave whole, 74 items in halves and 12 in pieces of three blocks; 198 (11 heads):
+# 49 items in thirds and 1 in pieces of two or three blocks.
+@pytest.mark.parametrize("b,h,s", [(1, 12, 4608), (1, 13, 4608), (1, 11, 4608)])
+def test_tiered_schedule_matches_unsplit(b, h, s):
+    """Shapes whose last wave would leave SMs idle keep the whole waves' items whole and cut the
+    rest over KV (two piece sizes): rows of whole items are bit-identical to the unsplit call,
+    the others equal it up to fp32 summation order, and all rows match the oracle."""
+    from flicker_b200 import _lib
+
+    items, whole, n_a, s_a, s_b, units = device_schedule(b, h, s)
+    if whole in (0, items):
+        pytest.skip("this device runs the shape without a tiered schedule")
+    lib = _lib.lib()
+    q, k, v = random_qkv(b, h, s, seed=5 + h)
+    qd, kd, vd = to_device(q), to_device(k), to_device(v)
+    ws_bytes = lib.flk_attend_workspace_size(b, h, s, 128)
+    assert ws_bytes > 0
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    o_tiered, o_plain = torch.empty_like(qd), torch.empty_like(qd)
+    assert lib.flk_attend(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), b, h, s, 128, o_tiered.data_ptr(),
+                          ws.data_ptr(), ws_bytes, None) == 0
+    assert lib.flk_attend(qd.data_ptr(), kd.data_ptr(), vd.data_ptr(), b, h, s, 128, o_plain.data_ptr(),
+                          None, 0, None) == 0
+    torch.cuda.synchronize()
+    a, p = to_host(o_tiered), to_host(o_plain)
+    n_pairs = (s // 128 + 1) // 2
+    first_split_row = (whole // n_pairs) * s + (whole % n_pairs) * 256  # items are (b, h)-major
+    flat_a, flat_p = a.reshape(-1, 128), p.reshape(-1, 128)
+    assert np.array_equal(flat_a[:first_split_row].view(np.uint16), flat_p[:first_split_row].view(np.uint16))
+    assert bit_equal_fraction(flat_a[first_split_row:], flat_p[first_split_row:]) > 0.97
+    rows = np.arange(0, s, max(1, s // 192))
+    want = R.attention_fp32(q, k, v, rows)
+    assert R.within_tolerance(a[:, :, rows], want)
+    assert R.within_tolerance(p[:, :, rows], want)
+    assert fb.device_status() == 0
+
+
 def test_many_calls_keep_status_and_results():
     """A soak of back-to-back calls: every barrier wait inside the kernels must keep ending (a
     wait that misses its phase ends only at its time limit and records a device timeout), and
     every call must reproduce the first one's output. 1500 calls at the 1024^2 shape (432 work
-    items on 148 persistent CTAs), then mixed shapes: split over KV, odd tile counts, one tile."""
+    items on 148 persistent CTAs), then mixed shapes: split over KV, odd tile counts, one tile,
+    a tiered schedule (whole items, then pieces of two sizes)."""
     def device_qkv(b, h, s, seed):
         g = torch.Generator(device="cuda")
         g.manual_seed(seed)
@@ -182,11 +233,12 @@ def test_many_calls_keep_status_and_results():
         same &= (fb.attend(q, k, v) == first).all()
     assert bool(same)
     assert fb.device_status() == 0
-    shapes = [device_qkv(1, 3, 4608, 22), device_qkv(2, 24, 1152, 23), device_qkv(3, 2, 128, 24)]
+    shapes = [device_qkv(1, 3, 4608, 22), device_qkv(2, 24, 1152, 23), device_qkv(3, 2, 128, 24),
+              device_qkv(1, 13, 4608, 25)]
     firsts = [fb.attend(*x) for x in shapes]
     for i in range(1000):
-        x = shapes[i % 3]
-        same &= (fb.attend(*x) == firsts[i % 3]).all()
+        x = shapes[i % 4]
+        same &= (fb.attend(*x) == firsts[i % 4]).all()
     assert bool(same)
     assert fb.device_status() == 0
 

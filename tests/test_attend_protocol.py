@@ -45,19 +45,36 @@ class Bar:
             self.completed += 1
 
 
-def decode(w, n_tiles, n_splits):
-    """decode_item (attend.cu): work item -> (query tiles, KV range)."""
+def schedule(n_tiles, n_splits, bh):
+    """(n_full, n_a, s_a, s_b) of AttendSchedule (attend_schedule.cuh) from a KV split count (every
+    item split that many ways) or such a tuple (whole items first, then two tiers of pieces)."""
+    n_items = bh * ((n_tiles + 1) // 2)
+    if isinstance(n_splits, tuple):
+        return n_splits
+    return (n_items, 0, 1, 1) if n_splits == 1 else (0, n_items, n_splits, n_splits)
+
+
+def decode(w, n_tiles, sched):
+    """decode_item (attend.cu): work unit -> (query tiles, KV range)."""
+    n_full, n_a, s_a, s_b = sched
     n_pairs = (n_tiles + 1) // 2
-    split = w % n_splits
-    pair = (w // n_splits) % n_pairs
-    t0 = pair * 2
-    kv0 = n_tiles * split // n_splits
-    return dict(w=w, nt=min(2, n_tiles - t0), n_kv=n_tiles * (split + 1) // n_splits - kv0)
+    if w < n_full:
+        item, split, splits = w, 0, 1
+    elif w - n_full < n_a * s_a:
+        item, split, splits = n_full + (w - n_full) // s_a, (w - n_full) % s_a, s_a
+    else:
+        u = w - n_full - n_a * s_a
+        item, split, splits = n_full + n_a + u // s_b, u % s_b, s_b
+    t0 = (item % n_pairs) * 2
+    kv0 = n_tiles * split // splits
+    return dict(w=w, nt=min(2, n_tiles - t0), n_kv=n_tiles * (split + 1) // splits - kv0)
 
 
 def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, release_from_tile0=False):
-    n_items = bh * ((n_tiles + 1) // 2) * n_splits
-    items = [decode(w, n_tiles, n_splits) for w in range(cta, n_items, grid)]
+    sched = schedule(n_tiles, n_splits, bh)
+    n_full, n_a, s_a, s_b = sched
+    n_units = n_full + n_a * s_a + (bh * ((n_tiles + 1) // 2) - n_full - n_a) * s_b
+    items = [decode(w, n_tiles, sched) for w in range(cta, n_units, grid)]
     q_full = Bar("q_full")
     kv_full = [Bar(f"kv_full{s}") for s in range(2)]
     s_full = [Bar(f"s_full{t}") for t in range(2)]
@@ -264,9 +281,12 @@ def run_cta(n_tiles, n_splits, bh, grid, cta, rng, p_hw=0.05, release_from_tile0
 
 
 # (tile count, KV splits, batch x heads, grid): even and odd tile counts (items of one and two
-# query tiles mixed), with and without KV splits, one or several items per CTA, single-block items.
+# query tiles mixed), with and without KV splits, one or several items per CTA, single-block items,
+# and tiered schedules (n_full, n_a, s_a, s_b): whole items, then pieces of two sizes, so one CTA
+# walks items of different lengths.
 CASES = [(2, 1, 2, 1), (3, 1, 2, 1), (4, 1, 3, 2), (5, 1, 3, 2), (6, 4, 1, 1), (7, 2, 3, 2), (8, 3, 3, 2),
-         (2, 2, 3, 1), (3, 3, 2, 1), (1, 1, 5, 2), (4, 4, 3, 2), (6, 6, 2, 3), (9, 1, 2, 1), (10, 1, 2, 1)]
+         (2, 2, 3, 1), (3, 3, 2, 1), (1, 1, 5, 2), (4, 4, 3, 2), (6, 6, 2, 3), (9, 1, 2, 1), (10, 1, 2, 1),
+         (6, (3, 2, 2, 3), 2, 3), (7, (2, 1, 3, 5), 2, 2), (8, (4, 1, 2, 2), 3, 4), (5, (3, 2, 2, 5), 2, 3)]
 
 
 @pytest.mark.parametrize("case", CASES)

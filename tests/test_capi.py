@@ -132,3 +132,46 @@ def test_shape_checks_run_before_any_device_work():
         == _lib.FLK_ERR_INVALID_ARGUMENT
     assert lib.flk_attend_merged(odd, fake, fake, 1, 2, 128, 128, fake, None, 0, None) \
         == _lib.FLK_ERR_INVALID_ARGUMENT
+
+
+def schedule(b, h, s, sms=148):
+    out = (ctypes.c_longlong * 6)()
+    assert _lib.lib().flk_attend_schedule(b, h, s, 128, sms, out) == 0
+    return tuple(out)
+
+
+def test_attend_schedule_host_query():
+    """The work schedule flk_attend uses (host-only query, no GPU): on a 148-SM B200 the 1024^2
+    call keeps its 432 items whole (three waves but for 12 idle SMs, too little to pay for a
+    combine), 3 heads split every item in two (one wave), 12 heads keep the first wave whole and
+    halve the last 68 items, 13 heads add a second tier of smaller pieces."""
+    assert schedule(1, 24, 4608) == (432, 432, 0, 1, 1, 432)
+    assert schedule(1, 3, 4608) == (54, 0, 54, 2, 2, 108)
+    assert schedule(1, 12, 4608) == (216, 148, 68, 2, 2, 284)
+    assert schedule(1, 13, 4608) == (234, 148, 74, 2, 12, 440)
+    assert schedule(1, 24, 1536) == (144, 144, 0, 1, 1, 144)
+    lib = _lib.lib()
+    out = (ctypes.c_longlong * 6)()
+    assert lib.flk_attend_schedule(1, 2, 200, 128, 148, out) == _lib.FLK_ERR_INVALID_ARGUMENT
+    assert lib.flk_attend_schedule(1, 2, 256, 64, 148, out) == _lib.FLK_ERR_UNSUPPORTED
+    assert lib.flk_attend_schedule(1, 2, 256, 128, 0, out) == _lib.FLK_ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("sms", [148, 132, 64])
+def test_attend_schedule_invariants(sms):
+    """For every shape: whole items fill whole waves (or all items), pieces are at least one KV
+    block, and under the persistent kernel's order (unit u on CTA u % sms) no CTA gets more than
+    one piece of each tier."""
+    for s in (128, 256, 1152, 1536, 4608, 8192, 16896):
+        n_tiles = s // 128
+        for b, h in ((1, 1), (1, 2), (1, 3), (1, 6), (1, 11), (1, 12), (1, 13), (1, 24), (2, 24), (8, 24)):
+            items, whole, n_a, s_a, s_b, units = schedule(b, h, s, sms)
+            assert items == b * h * ((n_tiles + 1) // 2)
+            rest = items - whole
+            assert units == whole + n_a * s_a + (rest - n_a) * s_b
+            assert 1 <= s_a <= n_tiles and 1 <= s_b <= n_tiles
+            if whole in (0, items):
+                continue
+            assert whole % sms == 0 and s_a >= 2 and n_a * s_a <= sms
+            if rest > n_a:
+                assert s_b >= 2 and (rest - n_a) * s_b <= sms

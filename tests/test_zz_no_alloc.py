@@ -4,12 +4,13 @@ Some callers of this library are handed only their input and output buffers and 
 for example an XLA custom-call handler registered without a scratch buffer, where the runtime
 owns all device memory and a cudaMalloc inside the handler would synchronise the device in the
 middle of XLA's asynchronous work. flk_attend needs caller-provided workspace when a shape runs
-split over KV; flk_attend_noalloc instead uses a 16 MiB scratch array built into the library.
+(partly) split over KV; flk_attend_noalloc instead uses a 32 MiB scratch array built into the
+library.
 
 These tests call both entry points through the C ABI and check that the allocation-free one
 gives the same result as flk_attend with a caller workspace, on two calls in a row (the scratch
 is shared by every call and keeps the previous call's contents), and that it refuses shapes
-whose split would need more than its 16 MiB.
+whose schedule would need more than its 32 MiB.
 
 This file is named so that pytest collects it last.
 """
@@ -57,7 +58,7 @@ def no_alloc(lib, q, k, v):
     return o
 
 
-@pytest.mark.parametrize("b,h,s", [(1, 3, 4608), (1, 2, 512), (2, 1, 1152), (1, 24, 1024)])
+@pytest.mark.parametrize("b,h,s", [(1, 3, 4608), (1, 2, 512), (2, 1, 1152), (1, 24, 1024), (1, 12, 4608)])
 def test_no_alloc_matches_workspace_entry_point_twice(b, h, s):
     lib = _lib.lib()
     first = qkv_inputs(b, h, s, seed=s + h)
@@ -74,13 +75,13 @@ def test_no_alloc_matches_workspace_entry_point_twice(b, h, s):
 
 def test_no_alloc_refuses_shapes_beyond_its_scratch():
     lib = _lib.lib()
-    # batch 1, 2 heads, S = 8192 runs split over KV on a 148-SM B200 and would need ~16.9 MB
-    # (> 16 MiB) of scratch. On a device with fewer SMs the shape may not split at all.
-    if lib.flk_attend_workspace_size(1, 2, 8192, 128) <= 16 << 20:
-        pytest.skip("this device runs the shape without a split over KV")
-    q, k, v = qkv_inputs(1, 2, 8192, seed=3)
+    # batch 1, 6 heads, S = 16896 (2048^2 on 4 GPUs) runs tiered on a 148-SM B200: two waves of
+    # whole items, then 74 items in halves and 26 in fifths, whose partials need ~36.7 MB
+    # (> 32 MiB) of scratch. On a device with another SM count the schedule may differ.
+    if lib.flk_attend_workspace_size(1, 6, 16896, 128) <= 32 << 20:
+        pytest.skip("this device's schedule for the shape fits the scratch")
+    q, k, v = qkv_inputs(1, 6, 16896, seed=3)
     o = torch.empty_like(q)
-    code = lib.flk_attend_noalloc(q.data_ptr(), k.data_ptr(), v.data_ptr(), 1, 2, 8192, 128, o.data_ptr(), None)
+    code = lib.flk_attend_noalloc(q.data_ptr(), k.data_ptr(), v.data_ptr(), 1, 6, 16896, 128, o.data_ptr(), None)
     assert code == _lib.FLK_ERR_WORKSPACE
-    assert lib.flk_attend_workspace_size(1, 2, 8192, 128) > 16 << 20
     assert lib.flk_device_status() == 0
