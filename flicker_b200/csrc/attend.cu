@@ -996,16 +996,19 @@ namespace {
 // Estimated cost of a schedule, in units of one 128-row KV block of one work unit (~2700 SM
 // cycles): the busiest CTA's blocks when unit u runs on CTA u % sms (the persistent kernel's
 // order; the one-unit-per-CTA kernel is dispatched in the same order), plus a fixed cost per unit
-// (its first S before any overlap, its epilogue) and per call (launch, ramp-up, drain), plus the
-// combine pass: a launch and the partials' traffic at ~9.75 MB of HBM per block time.
-constexpr double kUnitBlocks = 0.5, kCallBlocks = 7.0, kCombineBlocks = 2.0, kBytesPerBlock = 9.75e6;
+// (its first S before any overlap, its epilogue; more for a piece, whose epilogue writes fp32
+// partials) and per call (launch, ramp-up, drain), plus the combine pass: a launch and the
+// partials' traffic (written and read back) at ~9.75 MB of HBM per block time. The constants are
+// fitted to measured calls at S = 4608 and 16896 (11, 12, 13 and 3, 6, 12 heads on 148 SMs).
+constexpr double kWholeBlocks = 0.5, kPieceBlocks = 2.0, kCallBlocks = 7.0, kCombineBlocks = 3.0,
+                 kBytesPerBlock = 9.75e6;
 
 double schedule_cost(const AttendSchedule& sch, int B, int H, int S, int sms) {
   const int n_tiles = S / kTile;
   const long long F = sch.n_full, A = static_cast<long long>(sch.n_a) * sch.s_a, U = sch.units();
-  const double size_f = n_tiles + kUnitBlocks;
-  const double size_a = (n_tiles + sch.s_a - 1) / sch.s_a + kUnitBlocks;
-  const double size_b = (n_tiles + sch.s_b - 1) / sch.s_b + kUnitBlocks;
+  const double size_f = n_tiles + kWholeBlocks;
+  const double size_a = (n_tiles + sch.s_a - 1) / sch.s_a + kPieceBlocks;
+  const double size_b = (n_tiles + sch.s_b - 1) / sch.s_b + kPieceBlocks;
   // number of units u in [lo, hi) with u % sms == c
   auto count = [&](long long lo, long long hi, int c) -> long long {
     auto upto = [&](long long n) { return n <= c ? 0 : (n - 1 - c) / sms + 1; };  // u in [0, n)
@@ -1018,8 +1021,8 @@ double schedule_cost(const AttendSchedule& sch, int B, int H, int S, int sms) {
   if (sch.split()) {
     const double slots = static_cast<double>(attend_workspace_bytes(B, H, S, sch)) / ((kDim + 1) * sizeof(float));
     const double rows = static_cast<double>(B) * H * S - item_row(sch.n_full, (n_tiles + 1) / 2, S);
-    // partial rows written (half of it hidden under the attention) and read back, bf16 rows out
-    cost += kCombineBlocks + (slots * (kDim + 1) * 4 * 1.5 + rows * kDim * 2) / kBytesPerBlock;
+    // partial rows written and read back, bf16 rows out
+    cost += kCombineBlocks + (slots * (kDim + 1) * 4 * 2.0 + rows * kDim * 2) / kBytesPerBlock;
   }
   return cost;
 }
@@ -1032,8 +1035,8 @@ double schedule_cost(const AttendSchedule& sch, int B, int H, int S, int sms) {
 // Tiered rule: the items that fill whole waves stay whole; of the rest, n_a are split s_a ways
 // (at most one piece per SM) and the others s_b <= 16 ways (at most one more piece per SM), so the last
 // wave is cut into pieces that end together instead of leaving SMs idle (216 items on 148 SMs:
-// 36 + 18 blocks on the busiest SM instead of 2 x 36). Taken when its estimated cost is at least
-// 5 % below the base rule's.
+// 36 + 18 blocks on the busiest SM instead of 2 x 36; measured 102 against 116 us). Taken when
+// its estimated cost is at least 5 % below the base rule's.
 AttendSchedule attend_schedule(int B, int H, int S, int sms) {
   AttendSchedule base = attend_unsplit(B, H, S);
   const int n_tiles = S / kTile;

@@ -37,11 +37,12 @@ def gather_call(q, k, v, outs, h_total, h0):
     assert code == 0, code
 
 
-# On 148 SMs: (24 heads in 2 shards of 12) and (26 in 2 of 13) run tiered (the first wave of items
-# whole, stored by the attention epilogue; the rest split over KV, stored by the combine kernel);
+# On 148 SMs: (24 heads in 2 shards of 12) and (14 at S=8192 in 2 of 7) run tiered (the first wave
+# of items whole, stored by the attention epilogue; the rest split over KV, stored by the combine
+# kernel);
 # (8 heads in 4 shards of 2) and (6 in 3 of 2, B=2) run split over KV, so the combine kernel does
 # all the gathering stores; (32 heads in 2 shards of 16) runs unsplit.
-@pytest.mark.parametrize("b,h,s,shards", [(1, 24, 4608, 2), (1, 26, 4608, 2), (1, 8, 1024, 4), (2, 6, 512, 3),
+@pytest.mark.parametrize("b,h,s,shards", [(1, 24, 4608, 2), (1, 14, 8192, 2), (1, 8, 1024, 4), (2, 6, 512, 3),
                                           (1, 32, 2048, 2)])
 def test_shards_gathered_into_every_buffer(b, h, s, shards):
     """Each shard's heads land at their columns of every buffer, exactly as the shard's own
@@ -69,9 +70,9 @@ def test_shards_gathered_into_every_buffer(b, h, s, shards):
 # the one-item-per-CTA kernel with its TMA-staged epilogue whenever some items are whole:
 # (1, 24, 4608) is 432 items on 148 CTAs, (2, 24, 1536) 288 items, (3, 2, 128) single-tile items,
 # (2, 24, 1152) nine tiles per head (items of two and of one query tile mixed); (1, 12, 4608) and
-# (1, 13, 4608) run tiered on 148 SMs (whole items, then pieces whose partials the combine adds).
+# (1, 7, 8192) run tiered on 148 SMs (whole items, then pieces whose partials the combine adds).
 @pytest.mark.parametrize("b,h,s", [(1, 24, 4608), (2, 24, 1536), (3, 2, 128), (1, 16, 2048), (2, 24, 1152),
-                                   (1, 12, 4608), (1, 13, 4608)])
+                                   (1, 12, 4608), (1, 7, 8192)])
 def test_attend_persistent_matches(b, h, s):
     """The persistent kernel (units walked by one CTA per SM, barriers counting across units)
     computes exactly what one CTA per unit computes: bit-identical outputs."""

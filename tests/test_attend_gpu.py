@@ -173,10 +173,10 @@ def device_schedule(b, h, s):
     return tuple(out)
 
 
-# 216 items (12 heads at S=4608) on 148 SMs: one wave whole, the last 68 items in halves; 234 items
-# (13 heads): one wave whole, 74 items in halves and 12 in pieces of three blocks; 198 (11 heads):
-# 49 items in thirds and 1 in pieces of two or three blocks.
-@pytest.mark.parametrize("b,h,s", [(1, 12, 4608), (1, 13, 4608), (1, 11, 4608)])
+# On 148 SMs: 216 items (12 heads at S=4608): one wave whole, the last 68 items in halves; 162
+# items (9 heads): one wave whole, 14 items in eighths; 224 items (7 heads at S=8192): one wave
+# whole, 74 items in halves and 2 in pieces of four blocks.
+@pytest.mark.parametrize("b,h,s", [(1, 12, 4608), (1, 9, 4608), (1, 7, 8192)])
 def test_tiered_schedule_matches_unsplit(b, h, s):
     """Shapes whose last wave would leave SMs idle keep the whole waves' items whole and cut the
     rest over KV (two piece sizes): rows of whole items are bit-identical to the unsplit call,
@@ -234,7 +234,7 @@ def test_many_calls_keep_status_and_results():
     assert bool(same)
     assert fb.device_status() == 0
     shapes = [device_qkv(1, 3, 4608, 22), device_qkv(2, 24, 1152, 23), device_qkv(3, 2, 128, 24),
-              device_qkv(1, 13, 4608, 25)]
+              device_qkv(1, 7, 8192, 25)]
     firsts = [fb.attend(*x) for x in shapes]
     for i in range(1000):
         x = shapes[i % 4]

@@ -144,11 +144,13 @@ def test_attend_schedule_host_query():
     """The work schedule flk_attend uses (host-only query, no GPU): on a 148-SM B200 the 1024^2
     call keeps its 432 items whole (three waves but for 12 idle SMs, too little to pay for a
     combine), 3 heads split every item in two (one wave), 12 heads keep the first wave whole and
-    halve the last 68 items, 13 heads add a second tier of smaller pieces."""
+    halve the last 68 items, 13 heads stay whole (the pieces would cost more than the idle SMs),
+    7 heads at S=8192 add a second tier of smaller pieces."""
     assert schedule(1, 24, 4608) == (432, 432, 0, 1, 1, 432)
     assert schedule(1, 3, 4608) == (54, 0, 54, 2, 2, 108)
     assert schedule(1, 12, 4608) == (216, 148, 68, 2, 2, 284)
-    assert schedule(1, 13, 4608) == (234, 148, 74, 2, 12, 440)
+    assert schedule(1, 13, 4608) == (234, 234, 0, 1, 1, 234)
+    assert schedule(1, 7, 8192) == (224, 148, 74, 2, 16, 328)
     assert schedule(1, 24, 1536) == (144, 144, 0, 1, 1, 144)
     lib = _lib.lib()
     out = (ctypes.c_longlong * 6)()
