@@ -3,7 +3,10 @@ torchrun, one process per GPU): qk_prep + attend on this rank's heads, gathered 
 epilogue's stores into every rank's symmetric-memory buffer (sharding.attend_gather_heads), and,
 for comparison, by attend + an NCCL all-gather + merge_heads. Every rank checks, on two
 consecutive calls, that both gathers agree bit for bit and match the single-GPU result over all
-heads within the attention tolerance."""
+heads within the attention tolerance. Two shapes: the 512^2 grid over 24 heads (per-rank calls
+split over KV), and the 1024^2 grid with 12 heads per rank, whose per-rank calls run the tiered
+schedule on a 148-SM B200 (the first wave of items whole and stored by the attention epilogue,
+the rest split over KV and stored by the combine kernel)."""
 from __future__ import annotations
 
 import datetime
@@ -24,7 +27,22 @@ def main() -> int:
     dev = torch.device("cuda", int(os.environ["LOCAL_RANK"]))
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
-    H, num_txt, gh = 24, 512, 32
+    ok, peers = True, []
+    for H, gh in ((24, 32), (12 * world, 64)):
+        shape_ok, peer = run_shape(rank, world, dev, H, 512, gh)
+        ok &= shape_ok
+        peers.append(peer)  # symmetric memory stays allocated until every rank is done
+    status = fb.device_status()
+    flag = torch.tensor([1 if (ok and status == 0) else 0], device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    peers.clear()
+    dist.destroy_process_group()
+    return 0 if int(flag.item()) == 1 else 1
+
+
+def run_shape(rank: int, world: int, dev: torch.device, H: int, num_txt: int, gh: int):
+    """Both gathers of one shape on two consecutive calls; returns (all checks passed, the
+    symmetric-memory buffers, which the caller releases after the last collective)."""
     S = num_txt + gh * gh
     h0, h1 = sharding.head_range(H, world, rank)
     peer = sharding.PeerOutput((1, S, H * 128), dev, dist.group.WORLD)
@@ -51,19 +69,15 @@ def main() -> int:
         same = bool(torch.equal(fused, nccl))
         close = (fused.float() - full.float()).abs().max().item() <= 2e-2
         ok &= same and close
-        print(f"rank {rank} step {step}: fused == nccl {same}, fused ~ full {close}", flush=True)
+        print(f"rank {rank} H={H} S={S} step {step}: fused == nccl {same}, fused ~ full {close}", flush=True)
         if mc is not None:
             mc_same = bool(torch.equal(mc, nccl))
             ok &= mc_same
-            print(f"rank {rank} step {step}: multicast == nccl {mc_same}", flush=True)
+            print(f"rank {rank} H={H} S={S} step {step}: multicast == nccl {mc_same}", flush=True)
         else:
-            print(f"rank {rank} step {step}: no NVLink multicast on this node", flush=True)
-    status = fb.device_status()
-    flag = torch.tensor([1 if (ok and status == 0) else 0], device=dev)
-    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
-    del peer
-    dist.destroy_process_group()
-    return 0 if int(flag.item()) == 1 else 1
+            print(f"rank {rank} H={H} S={S} step {step}: no NVLink multicast on this node", flush=True)
+    torch.cuda.synchronize()
+    return ok, peer
 
 
 if __name__ == "__main__":

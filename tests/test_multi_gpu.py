@@ -33,7 +33,7 @@ def run_worker(n: int) -> None:
     res = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True)
     print(res.stdout[-3000:], res.stderr[-3000:])
     assert res.returncode == 0
-    assert res.stdout.count("fused == nccl True, fused ~ full True") == 2 * n
+    assert res.stdout.count("fused == nccl True, fused ~ full True") == 4 * n  # 2 shapes x 2 steps per rank
 
 
 def test_head_sharded_gather_on_two_gpus():
