@@ -175,8 +175,10 @@ def device_schedule(b, h, s):
 
 # On 148 SMs: 216 items (12 heads at S=4608): one wave whole, the last 68 items in halves; 162
 # items (9 heads): one wave whole, 14 items in eighths; 224 items (7 heads at S=8192): one wave
-# whole, 74 items in halves and 2 in pieces of four blocks.
-@pytest.mark.parametrize("b,h,s", [(1, 12, 4608), (1, 9, 4608), (1, 7, 8192)])
+# whole, 74 items in halves and 2 in pieces of four blocks; the same 216 items over batch
+# elements (2 x 6 heads), and with an odd tile count per head (3 x 4 heads at S=4480: items of
+# one query tile among the split ones).
+@pytest.mark.parametrize("b,h,s", [(1, 12, 4608), (1, 9, 4608), (1, 7, 8192), (2, 6, 4608), (3, 4, 4480)])
 def test_tiered_schedule_matches_unsplit(b, h, s):
     """Shapes whose last wave would leave SMs idle keep the whole waves' items whole and cut the
     rest over KV (two piece sizes): rows of whole items are bit-identical to the unsplit call,
