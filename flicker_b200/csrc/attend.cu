@@ -877,13 +877,30 @@ __global__ void __launch_bounds__(256) combine_splits_kernel(const float* __rest
   const long long stride = tier_a ? c.pa1 - c.pa0 : c.pb1 - c.pa1;
   float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float l = 0.f;
-  for (int s = 0; s < n; ++s) {
-    const long long slot = first + s * stride;
-    const float4* src = reinterpret_cast<const float4*>(acc + slot * kDim + col);
-    const float4 x = src[0], y = src[1];
-    a[0] += x.x; a[1] += x.y; a[2] += x.z; a[3] += x.w;
-    a[4] += y.x; a[5] += y.y; a[6] += y.z; a[7] += y.w;
-    l += lsum[slot];
+  // Up to four pieces' loads in flight at once (written by the previous kernel, read-only here),
+  // then added in piece order, as one piece at a time would.
+  constexpr int kBatch = 4;
+  for (int s0 = 0; s0 < n; s0 += kBatch) {
+    float4 x[kBatch], y[kBatch];
+    float ls[kBatch];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      if (s0 + i < n) {
+        const long long slot = first + (s0 + i) * stride;
+        const float4* src = reinterpret_cast<const float4*>(acc + slot * kDim + col);
+        x[i] = __ldg(src);
+        y[i] = __ldg(src + 1);
+        ls[i] = __ldg(lsum + slot);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      if (s0 + i < n) {
+        a[0] += x[i].x; a[1] += x[i].y; a[2] += x[i].z; a[3] += x[i].w;
+        a[4] += y[i].x; a[5] += y[i].y; a[6] += y[i].z; a[7] += y[i].w;
+        l += ls[i];
+      }
+    }
   }
   uint32_t pk[4];
   const float rl = __frcp_rn(l);
