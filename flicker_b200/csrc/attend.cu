@@ -1054,7 +1054,7 @@ double schedule_cost(const AttendSchedule& sch, int B, int H, int S, int sms) {
 // wave is cut into pieces that end together instead of leaving SMs idle (216 items on 148 SMs:
 // 36 + 18 blocks on the busiest SM instead of 2 x 36; measured 102 against 116 us). Taken when
 // its estimated cost is at least 5 % below the base rule's.
-AttendSchedule attend_schedule(int B, int H, int S, int sms) {
+static AttendSchedule compute_schedule(int B, int H, int S, int sms) {
   AttendSchedule base = attend_unsplit(B, H, S);
   const int n_tiles = S / kTile;
   const long long items = base.n_items;
@@ -1085,6 +1085,24 @@ AttendSchedule attend_schedule(int B, int H, int S, int sms) {
     if (cost < best_cost) best = c, best_cost = cost;
   }
   return best_cost < 0.95 * base_cost ? best : base;
+}
+
+// The rule costs a few to ~20 us of host time (a scan of the CTAs per candidate); every call asks
+// for it, so each host thread keeps its last few answers.
+AttendSchedule attend_schedule(int B, int H, int S, int sms) {
+  struct Entry {
+    int B = 0, H = 0, S = -1, sms = 0;
+    AttendSchedule sch;
+  };
+  constexpr int kEntries = 8;
+  thread_local Entry cache[kEntries];
+  thread_local unsigned next = 0;
+  for (const Entry& e : cache)
+    if (e.B == B && e.H == H && e.S == S && e.sms == sms) return e.sch;
+  Entry& e = cache[next++ % kEntries];
+  e.B = B, e.H = H, e.S = S, e.sms = sms;
+  e.sch = compute_schedule(B, H, S, sms);
+  return e.sch;
 }
 
 int launch_attend_out(const uint16_t* q, const uint16_t* k, const uint16_t* v, int B, int H, int S,
