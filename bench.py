@@ -719,12 +719,7 @@ def run_projection(args, rank, world):
 def preroll(torch):
     """Keep the GPU busy for ~10-15 ms (a spin kernel of torch's) before a timed region starts, so
     the host enqueues the first steps while it spins: with the queue ahead of the GPU, the events
-    between kernels measure the kernels, not the host's per-call time. Python's garbage collector
-    is run first and then switched off for the rest of this short-lived process: a collection
-    pausing the host for longer than the spin, between a step's first event and its launch, once
-    put a ~5 ms idle gap into one step's qk_prep window (mean 275.8 us against a median of 34.8)."""
-    gc.collect()
-    gc.disable()
+    between kernels measure the kernels, not the host's per-call time."""
     torch.cuda._sleep(25_000_000)
 
 
@@ -911,6 +906,12 @@ def measure_attention(args, torch, dist, fb, sharding, world, rank, dev, group, 
 
 
 def main():
+    # No automatic garbage collection in this short-lived process: a collection pausing the host
+    # for longer than the pre-roll spin, between a step's first event and its launch, once put a
+    # ~5 ms idle gap into one step's qk_prep window (mean 275.8 us against a median of 34.8). The
+    # switch is made once, up front: a collection started right before a timed region instead
+    # took different times on different ranks and put the skew into the first step's barrier.
+    gc.disable()
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -1037,8 +1038,6 @@ def main():
             }
             line["gpu_launches"] += (3 if hs["split"] else 2) * hs["K"]
     if world > 1:
-        import gc
-
         m = hs = None
         gc.collect()  # release the symmetric-memory buffers before the group goes away
         dist.barrier()
