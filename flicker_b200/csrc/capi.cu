@@ -127,7 +127,7 @@ int* current_device_status(int* err) {
 
 extern "C" {
 
-int flk_abi_version(void) { return 100; }
+int flk_abi_version(void) { return 101; }  // 1.01: flk_attend_schedule added
 
 const char* flk_error_string(int code) {
   switch (code) {
